@@ -1,0 +1,151 @@
+/* C ABI of the B200 (sm_100a) kernels for the trellis-coded W2A8 Linear.
+ *
+ * Drop-in boundary for the reference's kernel wrappers (ForeverBlue816/yanlongvla, deploy/tcq_kernels/kernels.py):
+ * each entry point below replaces one Python wrapper of that file (cited per function), keeps its argument meaning,
+ * and adds the shapes and the stream the wrapper used to read from tensors / torch.cuda.current_stream().
+ *
+ * Conventions (all entry points):
+ *   - every buffer is a device pointer allocated and owned by the caller; the library allocates nothing and keeps no
+ *     per-call state, so calls can be captured in a CUDA graph;
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream);
+ *   - optional outputs / inputs may be NULL where stated (the reference passes None for them, cuda_rt.py:90-91);
+ *   - BF16 values are passed as uint16_t bit patterns; dtype codes are TCQ_DT_*;
+ *   - the return value is a tcq_status: 0 on success; shapes and alignment are validated on the host before any
+ *     launch, so a non-zero status means nothing was launched (TCQ_ERR_LAUNCH: the launch itself failed).
+ */
+#ifndef TCQ_B200_H
+#define TCQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TCQ_ABI_VERSION 1
+
+enum tcq_status {
+    TCQ_OK = 0,
+    TCQ_ERR_SHAPE = 1,     /* a size is not supported (e.g. width not a multiple of 16, or above the limit)   */
+    TCQ_ERR_ALIGN = 2,     /* a pointer or leading dimension breaks the 16-byte alignment the kernel needs     */
+    TCQ_ERR_DTYPE = 3,     /* unknown dtype code                                                              */
+    TCQ_ERR_ARG = 4,       /* a required pointer is NULL, or an argument is out of range                        */
+    TCQ_ERR_LAUNCH = 5,    /* the CUDA launch failed (cudaGetLastError after the launch)                        */
+    TCQ_ERR_DEVICE = 6,    /* no usable device, or not an sm_100 device                                         */
+    TCQ_ERR_WORKSPACE = 7  /* the workspace is missing or smaller than the *_workspace() query returned           */
+};
+
+enum tcq_dtype { TCQ_DT_BF16 = 0, TCQ_DT_F32 = 1, TCQ_DT_F16 = 2, TCQ_DT_I32 = 3 };
+
+/* Library version and status text. */
+int tcq_abi_version(void);
+const char* tcq_status_string(int status);
+
+/* ------------------------------------------------------------------------------------------------ rotation + quantizer
+ * Row widths K / N are multiples of 16 and at most 16384; rows are rotated by the block Walsh over the binary
+ * decomposition of the width (tcq_format.py:26-55). */
+
+/* Replaces kernels.pre (kernels.py:602-606; kernel k_pre_*, kernels.py:208-219): x (M, K) BF16/F16/F32 -> sign flip
+ * by su (K,), block Walsh, per-token absmax INT8. Outputs q (M, K) int8 and/or q4 (K/4, ldq) int32 words (4
+ * consecutive inputs per word, token = column; NULL = not written), scale (M,) float32. */
+int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4, float* scale,
+            int M, int K, int ldq, void* stream);
+
+/* Replaces kernels.pre2 (kernels.py:631-633; k_pre2, kernels.py:295-307): x = BF16(g * u) of two BF16 (M, K) inputs,
+ * then as tcq_pre. */
+int tcq_pre2(const uint16_t* g, const uint16_t* u, const int8_t* su, int8_t* q, int32_t* q4, float* scale,
+             int M, int K, int ldq, void* stream);
+
+/* Replaces kernels.pre_h (kernels.py:677-680; k_preh_*, kernels.py:309-317): rotated activations as BF16, h (M, K)
+ * row-major and/or hT (K, ldh) with token = column. */
+int tcq_pre_h(const void* x, int x_dtype, const int8_t* su, uint16_t* h, uint16_t* hT, int M, int K, int ldh,
+              void* stream);
+
+/* Replaces kernels.post (kernels.py:612-615; k_post_*, kernels.py:221-230): for token t, columns col0 .. col0+N of
+ * the accumulator row acc (M, lda): z = ((float)a * s[t]) * rs[i] (acc_dtype I32), a (F32, already scaled) or
+ * bf2f(a) * rs[i] (BF16); then block Walsh, * sv[i], + bias[i] (bias may be NULL), BF16 y (M, N).
+ * s and rs may be NULL when acc_dtype does not use them. */
+int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+             uint16_t* y, int M, int N, int lda, int col0, void* stream);
+
+/* Replaces kernels.post3 (kernels.py:618-621; k_post3_*, kernels.py:232-247): three layers (q / k / v) sharing the
+ * accumulator row, columns [0,n0), [n0,n0+n1), [n0+n1, n0+n1+n2); rs / sv / bias concatenated. */
+int tcq_post3(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+              uint16_t* y0, uint16_t* y1, uint16_t* y2, int M, int n0, int n1, int n2, int lda, void* stream);
+
+/* Replaces kernels.postg (kernels.py:624-628; k_postg_*, kernels.py:249-261): up to three layers sharing the row, one
+ * thread block per (token, layer); act0 != 0 applies the activation table lut (65536 BF16 entries indexed by the BF16
+ * bit pattern) to the first layer's output. Unused layers: n = 0 and y = NULL. */
+int tcq_postg(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+              const uint16_t* lut, uint16_t* y0, uint16_t* y1, uint16_t* y2, int M, int n0, int n1, int n2, int lda,
+              int act0, void* stream);
+
+/* Replaces kernels.mid2 (kernels.py:641-644; k_mid2_*, kernels.py:263-278): gated-MLP middle. acc (M, lda) holds
+ * gate | up (columns [0,N) and [N,2N)); rs, sv concatenated (2N); g = lut(BF16(post(gate))), u = BF16(post(up)),
+ * x = BF16(g * u), then sign su (N,), block Walsh and INT8 quantizer as tcq_pre. lut = GELU-tanh (Gemma) or SiLU
+ * (SwiGLU) table. */
+int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const uint16_t* lut,
+             const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int N, int lda, int ldq, void* stream);
+
+/* Replaces kernels.mid1 (kernels.py:647-650; k_mid1_*, kernels.py:280-292): plain-MLP middle,
+ * x = lut(BF16(post(acc) + bias)) -> sign su, block Walsh, INT8. */
+int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+             const uint16_t* lut, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int N, int lda,
+             int ldq, void* stream);
+
+/* Standalone randomized Walsh rotation (the rotation op; tcq_format.py:44-55 with the signs of :130 / :145):
+ * forward y = fwht(x * signs), inverse y = fwht(x) * signs; x (M, D) BF16/F16/F32, y (M, D) BF16 or F32. */
+int tcq_rotate(const void* x, int x_dtype, const int8_t* signs, void* y, int y_dtype, int M, int D, int inverse,
+               void* stream);
+
+/* ------------------------------------------------------------------------------------------------ trellis weights
+ * bits: (m/16 * n/16, 32) uint16 words, 512 bits per 16 x 16 tile, tiles row-major (tcq_format.py:3-12, 58-63);
+ * t8: (512, 2) int8 table (tcq_format.py:74-77); m, n multiples of 16. */
+
+/* Replaces kernels.decode (kernels.py:653-656; k_decode, kernels.py:339-349): dense INT8 W (m, n) row-major. */
+int tcq_decode(const uint16_t* bits, const int8_t* t8, int8_t* out, int m, int n, void* stream);
+
+/* Replaces kernels.decode_bf16 (kernels.py:683-686; k_decode_bf16, kernels.py:320-337): tb (512, 2) BF16 bit
+ * patterns of the INT8 table values; out (m, n) BF16. */
+int tcq_decode_bf16(const uint16_t* bits, const uint16_t* tb, uint16_t* out, int m, int n, void* stream);
+
+/* Replaces kernels.gemm_w8 (kernels.py:662-668; k_gemm_w8, kernels.py:365-399): INT8-resident small-M product.
+ * W (N, K) int8, q4 (K/4, M) int32 words, s (M,), rs (N,) -> z (M, N) float32 = ((float)acc * s[t]) * rs[n].
+ * 1 <= M <= 16. */
+int tcq_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const float* rs, float* z, int M, int N, int K,
+                void* stream);
+
+/* Workspace of tcq_gemm_tcq in bytes for (M, N). The workspace must be zero-filled before its first use; every
+ * successful call leaves it zero-filled again. */
+size_t tcq_gemm_tcq_workspace(int M, int N);
+
+/* Replaces kernels.gemm_tcq (kernels.py:671-673; k_gemm_tcq, kernels.py:403-427): trellis decode fused into the
+ * small-M product; the decoded weights never leave the SM. Up to three layers concatenated along the output rows
+ * (q / k / v, gate / up): tile rows < nb0 use table 0 of t8 (3 x 1024 bytes), < nb1 table 1, else table 2
+ * (nb = 1 << 30: unused). z (M, N) float32 = ((float)acc * s[t]) * rs[n], bit-exact. 1 <= M <= 16.
+ * workspace: tcq_gemm_tcq_workspace(M, N) bytes, see above. */
+int tcq_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
+                 int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------ W8A8 INT8 GEMM
+ * q (M, K) int8 row-major (tokens), W (N, K) int8 row-major (output channels); K a multiple of 16; q, W 16-byte
+ * aligned. tcgen05 tensor cores (kind::i8), exact INT32 accumulation. */
+
+/* Replaces torch._int_mm(q, W.t()) as the reference calls it (modules.py:86; tcq_format.py:110-116):
+ * acc (M, N) int32 = q W^T, exact. */
+int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int K, void* stream);
+
+/* The reference's product + scale epilogue in one launch (tcq_format.py:135):
+ * out (M, N) = ((float)acc * s_tok[t]) * s_ch[n] as BF16 (out_dtype TCQ_DT_BF16) or FP32 (TCQ_DT_F32). */
+int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype,
+                  int M, int N, int K, void* stream);
+
+/* Device error flags raised by bounded waits inside the kernels (1 = a pipeline wait expired and the kernel stopped
+ * early). Synchronizes the current device. reset != 0 clears the flags. Returns -1 if the flags cannot be read. */
+int tcq_device_error(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCQ_B200_H */

@@ -108,9 +108,10 @@ def lookup(states, table):
 
 
 def snap(tlut_f16, row_scale_f16):
-    """INT8 table at load: g = 127 / max|tlut| (FP32), t8 = clamp(round(tlut * g)), rs = row_scale / g (tcq_format.py:74-77)."""
+    """INT8 table at load: g = 127 / max|tlut| (FP32), t8 = clamp(round(tlut * g)), rs = row_scale / g (tcq_format.py:74-77).
+    `127.0 / tensor` in PyTorch is `tensor.reciprocal() * 127.0`, so g = fl(fl(1 / max) * 127), not a true division."""
     t = np.asarray(tlut_f16, dtype=np.float16).astype(np.float32)
-    g = np.float32(np.float32(127.0) / np.abs(t).max())
+    g = np.float32(np.float32(np.float32(1.0) / np.abs(t).max()) * np.float32(127.0))
     t8 = np.clip(np.rint(t * g), -127, 127).astype(np.int8)
     rs = np.asarray(row_scale_f16, dtype=np.float16).astype(np.float32) / g
     return t8, rs.astype(np.float32), g

@@ -27,6 +27,17 @@ ROTATIONS = [(1, 16), (3, 48), (2, 1024), (5, 1152), (64, 4096), (2, 4304), (1, 
 GEMMS = [(1, 2048, 2048), (16, 2048, 6144), (64, 2048, 2048), (16, 8192, 2048), (3, 80, 48)]
 
 
+SNAP_TABLES = 64
+
+
+def snap_inputs(i):
+    """Table and row scales for the load-time INT8 snap (tcq_format.py:74-77): tables of varied scale."""
+    r = rng('snap', i)
+    tlut = (r.standard_normal((512, 2)) * r.uniform(0.2, 3.0)).astype(np.float16)
+    rsc = r.uniform(0.001, 0.05, size=64).astype(np.float16)
+    return tlut, rsc
+
+
 def rng(*key):
     seed = 0
     for k in key:

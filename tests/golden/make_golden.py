@@ -76,6 +76,12 @@ def main():
                 put(f'{name}/M{M}/y_fp16table_a16', bf16_np(F.reference_linear(xt, L, a8=False, table='fp16')))
         print(name, 'done', flush=True)
 
+    for i in range(cases.SNAP_TABLES):
+        tlut, rsc = cases.snap_inputs(i)
+        t8, rs, g = F.snap(torch.from_numpy(tlut), torch.from_numpy(rsc))
+        put(f'snap/{i}/t8', t8.numpy()); put(f'snap/{i}/rs', rs.numpy()); put(f'snap/{i}/gain', np.float32(g).reshape(1))
+    print('snap done', flush=True)
+
     for T, D in cases.ROTATIONS:
         x, s = cases.rotation_input(T, D)
         fwd = F.fwht(t_bits(x).float() * torch.from_numpy(s).float())

@@ -1,0 +1,87 @@
+"""W8A8 INT8 GEMM on tcgen05 (through the C ABI) against the CPU oracle: exact INT32 accumulators and bit-exact
+scale epilogues, including shapes whose K and N are not multiples of the 128-wide tiles (TMA zero fill)."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import golden
+import tcq_oracle as O
+from gpu_util import n, t
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip('no CUDA device')
+    from yanlongvla_b200 import kernels
+    kernels.device_error(reset=True)
+    yield kernels
+    assert kernels.device_error(reset=True) == 0, 'a kernel pipeline wait expired'
+
+
+def _rand(M, Kd, N, seed):
+    r = cases.rng('i8', M, Kd, N, seed)
+    q = r.integers(-127, 128, size=(M, Kd), dtype=np.int32).astype(np.int8)
+    w = r.integers(-127, 128, size=(N, Kd), dtype=np.int32).astype(np.int8)
+    return q, w
+
+
+@pytest.mark.parametrize('M,Kd,N', [(1, 128, 128), (3, 80, 48), (17, 1152, 320), (64, 2048, 2048), (100, 4304, 1152),
+                                    (256, 2048, 6144), (300, 1536, 1536), (513, 2048, 384), (1024, 8192, 2048)])
+def test_int_mm_exact(K, M, Kd, N):
+    q, w = _rand(M, Kd, N, 0)
+    acc = K.int_mm(t(q), t(w))
+    torch.cuda.synchronize()
+    ref = O.int_matmul(q, w)
+    assert np.array_equal(n(acc), ref), f'{int((n(acc) != ref).sum())} mismatches'
+
+
+def test_int_mm_extremes(K):
+    """All-(-127) and all-127 operands: the largest magnitudes the int8 path sees (no saturation, exact INT32)."""
+    M, Kd, N = 40, 8192, 256
+    q = np.full((M, Kd), -127, dtype=np.int8)
+    w = np.full((N, Kd), 127, dtype=np.int8)
+    w[::2] = -127
+    acc = n(K.int_mm(t(q), t(w)))
+    assert np.array_equal(acc, O.int_matmul(q, w))
+
+
+@pytest.mark.parametrize('M,Kd,N', cases.GEMMS)
+def test_int8_gemm_config3_golden(K, M, Kd, N):
+    """per-token quantizer (tcq_pre on an identity rotation is not the path here: the quantizer is
+    applied by the oracle) + tcgen05 GEMM + scale epilogue == the reference's BF16 output."""
+    a, w, sc = cases.gemm_inputs(M, Kd, N)
+    q, s = O.quantize_tokens(O.bf16_to_f32(a))
+    out = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc))
+    golden.check(f'gemm/{M}x{Kd}x{N}/out', n(out))
+    acc = K.int_mm(t(q), t(w))
+    golden.check(f'gemm/{M}x{Kd}x{N}/acc', n(acc))
+    z = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc), out_dtype=torch.float32)
+    assert np.array_equal(n(z), O.scale_acc(O.int_matmul(q, w), s[:, 0], sc))
+
+
+def test_int_mm_repeated_and_graph(K):
+    """Persistent tile loop across calls, and capture into a CUDA graph."""
+    M, Kd, N = 512, 2048, 2048
+    q, w = _rand(M, Kd, N, 1)
+    qd, wd = t(q), t(w)
+    ref = O.int_matmul(q, w)
+    out = torch.empty(M, N, dtype=torch.int32, device='cuda')
+    for _ in range(5):
+        K.int_mm(qd, wd, out=out)
+    assert np.array_equal(n(out), ref)
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        K.int_mm(qd, wd, out=out)
+    torch.cuda.current_stream().wait_stream(st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        K.int_mm(qd, wd, out=out)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert np.array_equal(n(out), ref)

@@ -64,6 +64,15 @@ def test_w8a8_gemm(M, K, N):
     golden.check(f'gemm/{M}x{K}x{N}/out', O.int8_gemm_scaled(q, w, s[:, 0], sc))
 
 
+@pytest.mark.parametrize('i', range(cases.SNAP_TABLES))
+def test_snap(i):
+    tlut, rsc = cases.snap_inputs(i)
+    t8, rs, g = O.snap(tlut, rsc)
+    golden.check(f'snap/{i}/t8', t8)
+    golden.check(f'snap/{i}/rs', rs)
+    golden.check(f'snap/{i}/gain', np.float32(g).reshape(1))
+
+
 def test_q4_layout():
     q = np.arange(-60, 60, dtype=np.int8).reshape(3, 40)
     w = O.q4_words(q)

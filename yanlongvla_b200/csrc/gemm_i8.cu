@@ -1,0 +1,385 @@
+// W8A8 INT8 GEMM on sm_100a: TMA -> 128B-swizzled shared memory -> tcgen05.mma.kind::i8 -> TMEM INT32 accumulators ->
+// tcgen05.ld epilogue with the per-token / per-channel scales.
+//
+// acc[t][c] = sum_k q[t][k] * W[c][k] (exact INT32), the product of the reference's prefill path
+// (torch._int_mm(q, W.t()), modules.py:86; tcq_format.py:110-116). Epilogues: raw INT32 (drop-in for _int_mm),
+// FP32 z = ((float)acc * s_tok[t]) * s_ch[c], or BF16(z) (tcq_format.py:135).
+//
+// Tiling: the UMMA M side is 128 output channels (rows of W), the UMMA N side BN tokens (32..256), K in 128-byte
+// stages (four K=32 MMAs per stage). One CTA per SM, persistent over tiles. Warp roles:
+//   warp 0    one thread issues the TMA loads (no multicast) into a STAGES-deep ring,
+//   warp 1    allocates TMEM; one thread issues tcgen05.mma and commits stage / accumulator barriers,
+//   warps 2-5 epilogue: tcgen05.ld of their 32-lane quarter, scale, coalesced stores; TMEM double-buffered so the
+//             epilogue of tile i overlaps the MMAs of tile i + 1.
+// Every mbarrier wait is bounded (about 2 s): on expiry the kernel sets a device error flag, stops, waits (bounded)
+// for its copies and MMAs in flight, frees TMEM and returns; tcq_device_error() reports the flag.
+#include <cuda.h>
+
+#include "tcq_common.cuh"
+
+__device__ int g_tcq_device_error;
+
+namespace {
+
+constexpr int BM = 128;           // channels per tile
+constexpr int BK = 128;           // K bytes per stage
+constexpr int kThreads = 192;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(u32 bar, u32 bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(u32 bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(u32 bar, u32 parity) {
+    u32 ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for the phase of parity `parity` to complete. Returns false when the CTA was aborted or the wait
+// expired (then the device error flag is set and the CTA abort flag raised).
+__device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, volatile int* abort_flag, unsigned long long limit = kWaitNs) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = gtime();
+    for (u32 i = 1;; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 127) == 0) {
+            if (*abort_flag) return false;
+            if (gtime() - t0 > limit) {
+                atomicOr(&g_tcq_device_error, 1);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(u32 dst, const CUtensorMap* map, u32 bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart
+// (SBO = 1024), LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B). The tile base is 1024-aligned, so
+// advancing along K inside the swizzle row is a plain add of 32 bytes to the start address.
+__device__ __forceinline__ u64 sw128_desc(u32 addr) {
+    return (u64)((addr >> 4) & 0x3FFF) | ((u64)1 << 16) | ((u64)(1024 >> 4) << 32) | ((u64)1 << 46) | ((u64)2 << 61);
+}
+
+// Instruction descriptor of tcgen05.mma.kind::i8: D s32, A and B signed int8, both K-major, N = bn, M = 128.
+__host__ __device__ constexpr u32 idesc_i8(int bn) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((u32)(bn >> 3) << 17) | ((u32)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(u32 d_tmem, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(u32 bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+enum { OUT_I32 = 0, OUT_F32 = 1, OUT_BF16 = 2 };
+
+template <int BN, int STAGES, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
+          const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K) {
+    constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
+    constexpr u32 TMEM_COLS = 2 * BN;          // two accumulator buffers; BN in {32, 64, 128, 256} -> power of two
+    constexpr u32 IDESC = idesc_i8(BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    u64* bars = reinterpret_cast<u64*>(sB + STAGES * B_BYTES);
+    u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * STAGES + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
+              tempty0 = smem_u32(bars + 2 * STAGES + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + BN - 1) / BN, tiles = tiles_n * tiles_m;
+    const int KB = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull0 + 8 * a, 1);
+            mbar_init(tempty0 + 8 * a, 128);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const u32 tmem = *tmem_slot;
+    pdl_launch_dependents();
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmW) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmQ) : "memory");
+            int stage = 0;
+            u32 phase = 0;
+            u32 armed[STAGES];
+            for (int s = 0; s < STAGES; ++s) armed[s] = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int tn = tile % tiles_n, tm = tile / tiles_n;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag)) { ok = false; break; }
+                    mbar_expect_tx(full0 + 8 * stage, A_BYTES + B_BYTES);
+                    tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmW, full0 + 8 * stage, kb * BK, tn * BM);
+                    tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmQ, full0 + 8 * stage, kb * BK, tm * BN);
+                    armed[stage] += 1;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (!ok) {
+                // Drain: wait (bounded) for the last load issued into every stage before shared memory goes away.
+                for (int s = 0; s < STAGES; ++s)
+                    if (armed[s]) { volatile int never = 0; mbar_wait(full0 + 8 * s, (armed[s] - 1) & 1, &never, 100000000ull); }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0, it = 0;
+            u32 phase = 0;
+            bool ok = true;
+            int committed = -1;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
+                const int a = it & 1;
+                const u32 aph = (it >> 1) & 1;
+                if (!mbar_wait(tempty0 + 8 * a, aph ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const u32 d = tmem + a * BN;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const u32 aaddr = smem_u32(sA + stage * A_BYTES), baddr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)
+                        mma_i8(d, sw128_desc(aaddr + 32 * k), sw128_desc(baddr + 32 * k), IDESC, (kb | k) != 0);
+                    mma_commit(empty0 + 8 * stage);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit(tfull0 + 8 * a);
+                committed = it;
+            }
+            if (!ok && committed >= 0) {
+                // MMAs already issued must finish before TMEM is freed: wait (bounded) for the last commit.
+                volatile int never = 0;
+                mbar_wait(tfull0 + 8 * (committed & 1), (committed >> 1) & 1, &never, 100000000ull);
+            }
+        }
+    } else {
+        const int q = warp & 3;                  // TMEM lane quarter this warp may access
+        int it = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+            const int a = it & 1;
+            const u32 aph = (it >> 1) & 1;
+            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
+            tc_fence_after();
+            const int tn = tile % tiles_n, tm = tile / tiles_n;
+            const int ch = tn * BM + 32 * q + lane, m0 = tm * BN;
+            const bool chok = ch < N;
+            const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                u32 v[32];
+                tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * BN + 32 * c), v);
+                const int t0 = m0 + 32 * c;
+                if (chok) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int tok = t0 + j;
+                        if (tok < M) {
+                            const size_t o = (size_t)tok * N + ch;
+                            if (MODE == OUT_I32) {
+                                reinterpret_cast<int*>(out)[o] = (int)v[j];
+                            } else {
+                                const float z = ((float)(int)v[j] * s_tok[tok]) * sc;
+                                if (MODE == OUT_F32) reinterpret_cast<float*>(out)[o] = z;
+                                else reinterpret_cast<u16*>(out)[o] = f2bf(z);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * a);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+int g_sms_i8 = 0;
+int sms() {
+    if (!g_sms_i8) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&g_sms_i8, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_sms_i8 <= 0) g_sms_i8 = 148;
+    }
+    return g_sms_i8;
+}
+
+// cuTensorMapEncodeTiled is a driver entry point; it is resolved through the runtime at first use so that the library
+// does not link libcuda (it loads on machines without a driver, where only the host-side validation is exercised).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D int8 tensor map over a row-major (rows, K) matrix: box = 128 bytes of K x box_rows rows, 128-byte swizzle,
+// out-of-bounds elements read as zero (exact for integer products).
+bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, int MODE>
+int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
+              cudaStream_t st) {
+    CUtensorMap tmW, tmQ;
+    if (!make_map(&tmW, W, N, K, BM) || !make_map(&tmQ, q, M, K, BN)) return TCQ_ERR_ARG;
+    auto kern = k_gemm_i8<BN, STAGES, MODE>;
+    const int smem = 1024 + STAGES * (BM + BN) * BK + (2 * STAGES + 4) * 8 + 16;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
+    const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
+    const int grid = tiles < sms() ? tiles : sms();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+}
+
+template <int MODE>
+int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
+             cudaStream_t st) {
+    if (M <= 32) return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
+    if (M <= 64) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
+    if (M <= 128) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
+    return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
+}
+
+int check_args(const int8_t* q, const int8_t* W, const void* out, int M, int N, int K) {
+    if (!q || !W || !out) return TCQ_ERR_ARG;
+    if (M <= 0 || N <= 0 || K <= 0 || (K & 15)) return TCQ_ERR_SHAPE;
+    if (!tcq_aligned(q, 16) || !tcq_aligned(W, 16)) return TCQ_ERR_ALIGN;
+    return TCQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int K, void* stream) {
+    const int e = check_args(q, W, acc, M, N, K);
+    if (e) return e;
+    return dispatch<OUT_I32>(q, W, acc, nullptr, nullptr, M, N, K, (cudaStream_t)stream);
+}
+
+int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype, int M,
+                  int N, int K, void* stream) {
+    const int e = check_args(q, W, out, M, N, K);
+    if (e) return e;
+    if (!s_tok || !s_ch) return TCQ_ERR_ARG;
+    if (out_dtype == TCQ_DT_BF16) return dispatch<OUT_BF16>(q, W, out, s_tok, s_ch, M, N, K, (cudaStream_t)stream);
+    if (out_dtype == TCQ_DT_F32) return dispatch<OUT_F32>(q, W, out, s_tok, s_ch, M, N, K, (cudaStream_t)stream);
+    return TCQ_ERR_DTYPE;
+}
+
+int tcq_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_tcq_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_tcq_device_error, &z, sizeof(int)) != cudaSuccess) return -1;
+    }
+    return v;
+}
+
+}  // extern "C"

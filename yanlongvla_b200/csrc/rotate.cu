@@ -1,0 +1,617 @@
+// Randomized block-Walsh rotation, per-token INT8 quantizer and the scale epilogue on sm_100a.
+//
+// One thread block per token row. A row of width K (multiple of 16, <= 16384) is the concatenation of descending
+// power-of-two blocks (tcq_format.py:26-30); each block gets the FP32 Walsh transform with stages h = 1, 2, 4, ...
+// and the scale (float)(1 / sqrt(w)) (tcq_format.py:44-55). The transform runs as radix-16 passes: the first pass
+// takes 16 contiguous inputs per thread straight from global memory (128-bit loads) and performs stages 1..8 in
+// registers; the later passes (stride 16, 256, 4096) go through shared memory in an XOR-swizzled layout that keeps
+// every 128-bit store and every 32-float warp access conflict-free. A radix-2^R pass performs exactly the additions
+// of R consecutive radix-2 stages in the same order, so the sums are bit-identical to the reference.
+#include "tcq_common.cuh"
+
+namespace {
+
+constexpr int kMaxWidth = 16384;
+
+// ---------------------------------------------------------------------------------------------------- row transform
+template <int R, class Fin>
+__device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bool last, Fin& fin) {
+    const int G = w >> R;
+    const float c = wscale(w);
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        const int low = g & (S - 1);
+        const int base = off + (((g - low) << R) | low);
+        float v[1 << R];
+#pragma unroll
+        for (int k = 0; k < (1 << R); ++k) v[k] = buf[swz(base + k * S)];
+        bfly<R>(v);
+        if (last) {
+#pragma unroll
+            for (int k = 0; k < (1 << R); ++k) fin(base + k * S, v[k] * c);
+        } else {
+#pragma unroll
+            for (int k = 0; k < (1 << R); ++k) buf[swz(base + k * S)] = v[k];
+        }
+    }
+}
+
+// ld16(c, v): the 16 inputs of chunk c (indices 16c .. 16c+15). fin(i, value): called exactly once per index with the
+// finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]).
+// Ends with a __syncthreads() so that values fin stored to buf are visible to the whole block.
+template <class Ld16, class Fin>
+__device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
+    const int nch = K >> 4;
+    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        float v[16];
+        ld16(c, v);
+        bfly<4>(v);
+        const int i0 = c << 4;
+        if (block_of(i0, K) == 16) {
+            const float sc = wscale(16);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) fin(i0 + k, v[k] * sc);
+        } else {
+            float4* b4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+    }
+    __syncthreads();
+    for (int S = 16;; S <<= 4) {
+        bool work = false;
+        int off = 0;
+        for (int rem = K; rem;) {
+            const int w = 1 << (31 - __clz(rem));
+            if (w > S) {
+                work = true;
+                const int L = 31 - __clz(w / S);
+                const bool last = L <= 4;
+                switch (last ? L : 4) {
+                    case 4: walsh_pass<4>(buf, off, w, S, last, fin); break;
+                    case 3: walsh_pass<3>(buf, off, w, S, last, fin); break;
+                    case 2: walsh_pass<2>(buf, off, w, S, last, fin); break;
+                    default: walsh_pass<1>(buf, off, w, S, last, fin); break;
+                }
+            }
+            off += w;
+            rem -= w;
+        }
+        __syncthreads();
+        if (!work) break;
+    }
+}
+
+__device__ __forceinline__ float block_max(float mx, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float r = 0.f;
+    const int warps = (blockDim.x + 31) >> 5;
+    for (int i = 0; i < warps; ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+
+// Per-token INT8 quantizer (tcq_format.py:119-122; kernels.py:164-184): s = amax / 127 (IEEE division, 1 when
+// amax = 0), q = clamp(rint(v / s), -127, 127). q (M, K) row-major and/or q4 (K/4, ldq) words, token = column.
+__device__ __forceinline__ int q8(float v, float s) {
+    float r = rintf(v / s);
+    r = fminf(fmaxf(r, -127.f), 127.f);
+    return (int)r;
+}
+
+__device__ __forceinline__ void quantize_store(const float* buf, float mx, float* red, int8_t* q, int* q4, float* scale,
+                                               int tok, int K, int ldq) {
+    mx = block_max(mx, red);
+    const float s = mx > 0.f ? mx / 127.f : 1.f;
+    if (threadIdx.x == 0) scale[tok] = s;
+    const float4* b4 = reinterpret_cast<const float4*>(buf);
+    for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
+        u32 w[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const float4 v = b4[swz(16 * c + 4 * g) >> 2];
+            w[g] = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
+                   ((u32)(q8(v.w, s) & 0xff) << 24);
+        }
+        if (q) *reinterpret_cast<uint4*>(q + (size_t)tok * K + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+        if (q4) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) q4[(size_t)(4 * c + g) * ldq + tok] = (int)w[g];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------- loaders
+// 16 inputs of a row (BF16 / F16 / F32), 16-byte aligned.
+template <int DT>
+__device__ __forceinline__ void load16(const void* p, float* v) {
+    if (DT == TCQ_DT_F32) {
+        const float4* f = reinterpret_cast<const float4*>(p);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 a = __ldg(f + q);
+            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+        }
+    } else {
+        const uint4* u = reinterpret_cast<const uint4*>(p);
+        const uint4 a = __ldg(u), b = __ldg(u + 1);
+        const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (DT == TCQ_DT_BF16) {
+                v[2 * k] = __uint_as_float(w[k] << 16);
+                v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+            } else {
+                v[2 * k] = h2f((u16)(w[k] & 0xffff));
+                v[2 * k + 1] = h2f((u16)(w[k] >> 16));
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void load_signs16(const i8* p, float* sg) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const u32 w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
+}
+
+__device__ __forceinline__ void load_f16x(const float* p, float* v) {
+    const float4* f = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 a = __ldg(f + q);
+        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+    }
+}
+
+// Scaled accumulator inputs z = SCALE(acc): I32 ((float)a * s) * rs, F32 a, BF16 bf2f(a) * rs (kernels.py:545).
+template <int AT>
+__device__ __forceinline__ void load_scaled16(const void* acc, size_t idx, float s, const float* rs, float* v) {
+    if (AT == TCQ_DT_I32) {
+        const int4* a4 = reinterpret_cast<const int4*>(reinterpret_cast<const int*>(acc) + idx);
+        float r[16];
+        load_f16x(rs, r);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int4 a = __ldg(a4 + q);
+            v[4 * q] = ((float)a.x * s) * r[4 * q];
+            v[4 * q + 1] = ((float)a.y * s) * r[4 * q + 1];
+            v[4 * q + 2] = ((float)a.z * s) * r[4 * q + 2];
+            v[4 * q + 3] = ((float)a.w * s) * r[4 * q + 3];
+        }
+    } else if (AT == TCQ_DT_F32) {
+        load_f16x(reinterpret_cast<const float*>(acc) + idx, v);
+    } else {
+        float r[16];
+        load_f16x(rs, r);
+        load16<TCQ_DT_BF16>(reinterpret_cast<const u16*>(acc) + idx, v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = v[k] * r[k];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------- kernels
+template <int DT>
+__global__ void __launch_bounds__(512) k_pre(const void* __restrict__ x, const i8* __restrict__ su, int8_t* __restrict__ q,
+                                             int* __restrict__ q4, float* __restrict__ scale, int M, int K, int ldq) {
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+    const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
+    float mx = 0.f;
+    row_walsh(buf, K,
+              [&](int c, float* v) {
+                  float sg[16];
+                  load16<DT>(xr + (size_t)16 * c * es, v);
+                  load_signs16(su + 16 * c, sg);
+#pragma unroll
+                  for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
+              },
+              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
+}
+
+__global__ void __launch_bounds__(512) k_pre2(const u16* __restrict__ g, const u16* __restrict__ u, const i8* __restrict__ su,
+                                              int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M,
+                                              int K, int ldq) {
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * K;
+    float mx = 0.f;
+    row_walsh(buf, K,
+              [&](int c, float* v) {
+                  float gv[16], uv[16], sg[16];
+                  load16<TCQ_DT_BF16>(g + base + 16 * c, gv);
+                  load16<TCQ_DT_BF16>(u + base + 16 * c, uv);
+                  load_signs16(su + 16 * c, sg);
+#pragma unroll
+                  for (int k = 0; k < 16; ++k) v[k] = bf2f(f2bf(gv[k] * uv[k])) * sg[k];
+              },
+              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(512) k_pre_h(const void* __restrict__ x, const i8* __restrict__ su, u16* __restrict__ h,
+                                               u16* __restrict__ hT, int M, int K, int ldh) {
+    extern __shared__ __align__(16) float buf[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+    const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
+    row_walsh(buf, K,
+              [&](int c, float* v) {
+                  float sg[16];
+                  load16<DT>(xr + (size_t)16 * c * es, v);
+                  load_signs16(su + 16 * c, sg);
+#pragma unroll
+                  for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
+              },
+              [&](int i, float v) {
+                  const u16 b = f2bf(v);
+                  if (h) h[(size_t)tok * K + i] = b;
+                  if (hT) hT[(size_t)i * ldh + tok] = b;
+              });
+}
+
+template <int DT, int OT>
+__global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, const i8* __restrict__ sg, void* __restrict__ y,
+                                                int M, int D, int inverse) {
+    extern __shared__ __align__(16) float buf[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+    const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * D * es;
+    row_walsh(buf, D,
+              [&](int c, float* v) {
+                  load16<DT>(xr + (size_t)16 * c * es, v);
+                  if (!inverse) {
+                      float s16[16];
+                      load_signs16(sg + 16 * c, s16);
+#pragma unroll
+                      for (int k = 0; k < 16; ++k) v[k] = v[k] * s16[k];
+                  }
+              },
+              [&](int i, float v) {
+                  if (inverse) v = v * (float)sg[i];
+                  if (OT == TCQ_DT_F32) reinterpret_cast<float*>(y)[(size_t)tok * D + i] = v;
+                  else reinterpret_cast<u16*>(y)[(size_t)tok * D + i] = f2bf(v);
+              });
+}
+
+// Epilogue of one layer on one token: SCALE(acc[base + i]) -> block Walsh -> * sv -> + bias -> BF16 (-> act).
+template <int AT, class Out>
+__device__ __forceinline__ void post_row(float* buf, const void* acc, size_t base, float s, const float* rs, const i8* sv,
+                                         const float* bias, int N, Out out) {
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, s, rs ? rs + 16 * c : nullptr, v); },
+              [&](int i, float v) {
+                  v = v * (float)sv[i];
+                  if (bias) v = v + bias[i];
+                  out(i, f2bf(v));
+              });
+}
+
+template <int AT>
+__global__ void __launch_bounds__(512) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+                                              const i8* __restrict__ sv, const float* __restrict__ bias, u16* __restrict__ y, int M,
+                                              int N, int lda, int col0) {
+    extern __shared__ __align__(16) float buf[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    u16* yo = y + (size_t)tok * N;
+    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rs, sv, bias, N, [&](int i, u16 b) { yo[i] = b; });
+}
+
+// Several layers sharing the accumulator row. grid.y == 1: the layers one after another in one block (post3);
+// grid.y == number of layers: one block per (token, layer) (postg). act0: activation table on layer 0's output.
+template <int AT>
+__global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc, const float* __restrict__ s,
+                                                    const float* __restrict__ rs, const i8* __restrict__ sv,
+                                                    const float* __restrict__ bias, const u16* __restrict__ lut, u16* y0, u16* y1,
+                                                    u16* y2, int M, int n0, int n1, int n2, int lda, int act0) {
+    extern __shared__ __align__(16) float buf[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const int seg_begin = gridDim.y == 1 ? 0 : blockIdx.y, seg_end = gridDim.y == 1 ? 3 : blockIdx.y + 1;
+    for (int seg = seg_begin; seg < seg_end; ++seg) {
+        const int N = seg == 0 ? n0 : seg == 1 ? n1 : n2;
+        if (N == 0) continue;
+        const int c0 = seg == 0 ? 0 : seg == 1 ? n0 : n0 + n1;
+        u16* yo = (seg == 0 ? y0 : seg == 1 ? y1 : y2) + (size_t)tok * N;
+        const bool act = act0 && seg == 0;
+        post_row<AT>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rs ? rs + c0 : nullptr, sv + c0,
+                     bias ? bias + c0 : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; });
+    }
+}
+
+// Gated-MLP middle (kernels.py:263-278): g = lut(BF16(post(gate))), u = BF16(post(up)), x = BF16(g * u) * su,
+// block Walsh, INT8. Shared memory: N floats + N BF16.
+template <int AT>
+__global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+                                              const i8* __restrict__ sv, const u16* __restrict__ lut, const i8* __restrict__ su,
+                                              int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M, int N,
+                                              int lda, int ldq) {
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    u16* gb = reinterpret_cast<u16*>(buf + N);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * lda;
+    const float st = s ? s[tok] : 1.f;
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rs ? rs + 16 * c : nullptr, v); },
+              [&](int i, float v) { gb[i] = lut[f2bf(v * (float)sv[i])]; });
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + N + 16 * c, st, rs ? rs + N + 16 * c : nullptr, v); },
+              [&](int i, float v) {
+                  const u16 u = f2bf(v * (float)sv[N + i]);
+                  buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)su[i];
+              });
+    float mx = 0.f;
+    row_walsh(buf, N,
+              [&](int c, float* v) {
+                  const float4* b4 = reinterpret_cast<const float4*>(buf);
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) {
+                      const float4 a = b4[swz(16 * c + 4 * g) >> 2];
+                      v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
+                  }
+              },
+              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
+// Plain-MLP middle (kernels.py:280-292): x = lut(BF16(post(acc) + bias)) * su, block Walsh, INT8.
+template <int AT>
+__global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+                                              const i8* __restrict__ sv, const float* __restrict__ bias, const u16* __restrict__ lut,
+                                              const i8* __restrict__ su, int8_t* __restrict__ q, int* __restrict__ q4,
+                                              float* __restrict__ scale, int M, int N, int lda, int ldq) {
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * lda;
+    const float st = s ? s[tok] : 1.f;
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rs ? rs + 16 * c : nullptr, v); },
+              [&](int i, float v) {
+                  v = v * (float)sv[i];
+                  if (bias) v = v + bias[i];
+                  buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)su[i];
+              });
+    float mx = 0.f;
+    row_walsh(buf, N,
+              [&](int c, float* v) {
+                  const float4* b4 = reinterpret_cast<const float4*>(buf);
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) {
+                      const float4 a = b4[swz(16 * c + 4 * g) >> 2];
+                      v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
+                  }
+              },
+              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
+// ---------------------------------------------------------------------------------------------------- host side
+int threads_for(int K) {
+    int t = ((K >> 4) + 31) & ~31;
+    if (t < 32) t = 32;
+    if (t > 512) t = 512;
+    return t;
+}
+
+bool width_ok(int K) { return K > 0 && (K & 15) == 0 && K <= kMaxWidth; }
+
+template <class Kern, class... Args>
+int launch(Kern kern, dim3 grid, int threads, size_t smem, void* stream, Args... args) {
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return TCQ_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+}
+
+bool acc_aligned(const void* acc, int acc_dtype, int lda, int col0) {
+    const int vec = acc_dtype == TCQ_DT_BF16 ? 8 : 4;   // elements per 16 bytes
+    return tcq_aligned(acc, 16) && lda % vec == 0 && col0 % vec == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tcq_abi_version(void) { return TCQ_ABI_VERSION; }
+
+const char* tcq_status_string(int status) {
+    switch (status) {
+        case TCQ_OK: return "ok";
+        case TCQ_ERR_SHAPE: return "unsupported shape";
+        case TCQ_ERR_ALIGN: return "misaligned pointer or leading dimension (16-byte alignment required)";
+        case TCQ_ERR_DTYPE: return "unknown dtype";
+        case TCQ_ERR_ARG: return "invalid argument";
+        case TCQ_ERR_LAUNCH: return "CUDA launch failed";
+        case TCQ_ERR_DEVICE: return "no usable sm_100 device";
+        case TCQ_ERR_WORKSPACE: return "workspace missing or too small";
+        default: return "unknown status";
+    }
+}
+
+int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int K, int ldq,
+            void* stream) {
+    if (!x || !su || !scale || (!q && !q4)) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(K)) return TCQ_ERR_SHAPE;
+    if (q4 && ldq < M) return TCQ_ERR_ARG;
+    if (!tcq_aligned(x, 16) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16))) return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)4 * K;
+    const int T = threads_for(K);
+    switch (x_dtype) {
+        case TCQ_DT_BF16: return launch(k_pre<TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+        case TCQ_DT_F16: return launch(k_pre<TCQ_DT_F16>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+        case TCQ_DT_F32: return launch(k_pre<TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+int tcq_pre2(const uint16_t* g, const uint16_t* u, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int K,
+             int ldq, void* stream) {
+    if (!g || !u || !su || !scale || (!q && !q4)) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(K)) return TCQ_ERR_SHAPE;
+    if (q4 && ldq < M) return TCQ_ERR_ARG;
+    if (!tcq_aligned(g, 16) || !tcq_aligned(u, 16) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16))) return TCQ_ERR_ALIGN;
+    return launch(k_pre2, dim3(M), threads_for(K), (size_t)4 * K, stream, (const u16*)g, (const u16*)u, (const i8*)su, q,
+                  (int*)q4, scale, M, K, ldq);
+}
+
+int tcq_pre_h(const void* x, int x_dtype, const int8_t* su, uint16_t* h, uint16_t* hT, int M, int K, int ldh, void* stream) {
+    if (!x || !su || (!h && !hT)) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(K)) return TCQ_ERR_SHAPE;
+    if (hT && ldh < M) return TCQ_ERR_ARG;
+    if (!tcq_aligned(x, 16) || !tcq_aligned(su, 16)) return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)4 * K;
+    const int T = threads_for(K);
+    switch (x_dtype) {
+        case TCQ_DT_BF16: return launch(k_pre_h<TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+        case TCQ_DT_F16: return launch(k_pre_h<TCQ_DT_F16>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+        case TCQ_DT_F32: return launch(k_pre_h<TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+int tcq_rotate(const void* x, int x_dtype, const int8_t* signs, void* y, int y_dtype, int M, int D, int inverse,
+               void* stream) {
+    if (!x || !signs || !y) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(D)) return TCQ_ERR_SHAPE;
+    if (!tcq_aligned(x, 16) || !tcq_aligned(signs, 16)) return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)4 * D;
+    const int T = threads_for(D);
+    const int inv = inverse ? 1 : 0;
+    if (y_dtype != TCQ_DT_F32 && y_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
+    const bool of = y_dtype == TCQ_DT_F32;
+    switch (x_dtype) {
+        case TCQ_DT_BF16:
+            return of ? launch(k_rotate<TCQ_DT_BF16, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                      : launch(k_rotate<TCQ_DT_BF16, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+        case TCQ_DT_F16:
+            return of ? launch(k_rotate<TCQ_DT_F16, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                      : launch(k_rotate<TCQ_DT_F16, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+        case TCQ_DT_F32:
+            return of ? launch(k_rotate<TCQ_DT_F32, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                      : launch(k_rotate<TCQ_DT_F32, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+             uint16_t* y, int M, int N, int lda, int col0, void* stream) {
+    if (!acc || !sv || !y) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_I32 && (!s || !rs)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(N) || col0 < 0 || lda < col0 + N) return TCQ_ERR_SHAPE;
+    if (!acc_aligned(acc, acc_dtype, lda, col0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)4 * N;
+    const int T = threads_for(N);
+    switch (acc_dtype) {
+        case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
+        case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
+        case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+static int post_multi(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+                      const uint16_t* lut, uint16_t* y0, uint16_t* y1, uint16_t* y2, int M, int n0, int n1, int n2, int lda,
+                      int act0, int per_layer_blocks, void* stream) {
+    if (!acc || !sv || !y0) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_I32 && (!s || !rs)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
+    if (act0 && !lut) return TCQ_ERR_ARG;
+    if ((n1 && !y1) || (n2 && !y2)) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(n0) || (n1 && !width_ok(n1)) || (n2 && !width_ok(n2)) || n1 < 0 || n2 < 0) return TCQ_ERR_SHAPE;
+    if (n2 && !n1) return TCQ_ERR_SHAPE;
+    if (lda < n0 + n1 + n2) return TCQ_ERR_SHAPE;
+    if (!acc_aligned(acc, acc_dtype, lda, 0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
+    const int nmax = n0 > n1 ? (n0 > n2 ? n0 : n2) : (n1 > n2 ? n1 : n2);
+    const int layers = 1 + (n1 > 0) + (n2 > 0);
+    const dim3 grid(M, per_layer_blocks ? layers : 1);
+    const size_t smem = (size_t)4 * nmax;
+    const int T = threads_for(nmax);
+    switch (acc_dtype) {
+        case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
+        case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
+        case TCQ_DT_BF16: return launch(k_post_multi<TCQ_DT_BF16>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+int tcq_post3(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+              uint16_t* y0, uint16_t* y1, uint16_t* y2, int M, int n0, int n1, int n2, int lda, void* stream) {
+    return post_multi(acc, acc_dtype, s, rs, sv, bias, nullptr, y0, y1, y2, M, n0, n1, n2, lda, 0, 0, stream);
+}
+
+int tcq_postg(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+              const uint16_t* lut, uint16_t* y0, uint16_t* y1, uint16_t* y2, int M, int n0, int n1, int n2, int lda, int act0,
+              void* stream) {
+    return post_multi(acc, acc_dtype, s, rs, sv, bias, lut, y0, y1, y2, M, n0, n1, n2, lda, act0, 1, stream);
+}
+
+int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const uint16_t* lut,
+             const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int N, int lda, int ldq, void* stream) {
+    if (!acc || !sv || !lut || !su || !scale || (!q && !q4)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_I32 && (!s || !rs)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(N) || lda < 2 * N) return TCQ_ERR_SHAPE;
+    if (q4 && ldq < M) return TCQ_ERR_ARG;
+    if (!acc_aligned(acc, acc_dtype, lda, N) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
+        return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)6 * N;
+    const int T = threads_for(N);
+    switch (acc_dtype) {
+        case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_BF16: return launch(k_mid2<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
+             const uint16_t* lut, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int N, int lda, int ldq,
+             void* stream) {
+    if (!acc || !sv || !lut || !su || !scale || (!q && !q4)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_I32 && (!s || !rs)) return TCQ_ERR_ARG;
+    if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
+    if (M <= 0 || !width_ok(N) || lda < N) return TCQ_ERR_SHAPE;
+    if (q4 && ldq < M) return TCQ_ERR_ARG;
+    if (!acc_aligned(acc, acc_dtype, lda, 0) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
+        return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)4 * N;
+    const int T = threads_for(N);
+    switch (acc_dtype) {
+        case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_BF16: return launch(k_mid1<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        default: return TCQ_ERR_DTYPE;
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,95 @@
+// Shared device helpers of the sm_100a trellis-coded W2A8 kernels.
+//
+// Bit-exactness contract (the same as the reference definition, deploy/tcq_kernels/tcq_format.py and kernels.py:8-10):
+// FP32 butterflies in stage order h = 1, 2, 4, ... with (a + b, a - b) pairs, block scale as an FP32 multiply by
+// (float)(1 / sqrt((double)w)), true FP32 division and round-half-even in the activation quantizer, the product
+// epilogue ((float)acc * s) * rs, BF16 by round-to-nearest-even. Every file is compiled with -fmad=false, so no
+// a * b + c is contracted into an FMA.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tcq_b200.h"
+
+typedef unsigned short u16;
+typedef unsigned int u32;
+typedef signed char i8;
+typedef unsigned long long u64;
+
+#define TCQ_HD __device__ __forceinline__
+
+// ---------------------------------------------------------------------------------------------------- BF16 / FP16
+TCQ_HD float bf2f(u16 b) { return __uint_as_float(((u32)b) << 16); }
+
+// FP32 -> BF16, round to nearest even; NaN -> 0x7fc0 (the c10::BFloat16 scalar rule, kernels.py:20-25).
+TCQ_HD u16 f2bf(float f) {
+    u32 u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (u16)0x7fc0;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (u16)(u >> 16);
+}
+
+TCQ_HD float h2f(u16 h) {
+    float f;
+    asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
+    return f;
+}
+
+// ---------------------------------------------------------------------------------------------------- Walsh helpers
+// FP32 block scale of a power-of-two width: (float)(1 / sqrt((double)w)) (tcq_format.py:36-41).
+TCQ_HD float wscale(int w) { return (float)(1.0 / sqrt((double)w)); }
+
+// R radix-2 stages on 2^R values in registers: stage s pairs slot k with k + 2^s, low slot gets a + b, high slot a - b.
+template <int R>
+TCQ_HD void bfly(float* v) {
+#pragma unroll
+    for (int s = 0; s < R; ++s) {
+        const int hh = 1 << s;
+#pragma unroll
+        for (int k = 0; k < (1 << R); ++k)
+            if (!(k & hh)) {
+                const float a = v[k], b = v[k + hh];
+                v[k] = a + b;
+                v[k + hh] = a - b;
+            }
+    }
+}
+
+// Width of the power-of-two block of a row of width K (K % 16 == 0, descending binary decomposition) that contains
+// index i < K: the highest bit in which i and K differ (i agrees with K above it and has a 0 there).
+TCQ_HD int block_of(int i, int K) { return 1 << (31 - __clz(i ^ K)); }
+
+// Shared-memory layout of a row being transformed: element i lives at swz(i). The XOR permutes the four 16-byte
+// granules of each 16-element chunk so that 32 lanes storing 16 contiguous floats each (4 x st.shared.v4) hit all 32
+// banks; 32 consecutive indices still map to 32 distinct banks.
+TCQ_HD int swz(int i) { return i ^ (((i >> 5) & 3) << 2); }
+
+// ---------------------------------------------------------------------------------------------------- loads
+TCQ_HD uint4 ldg_nc_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// Streaming load that does not allocate in L1 (the 2-bit weight stream is read exactly once per launch).
+TCQ_HD uint4 ldg_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// ---------------------------------------------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute may start while its
+// predecessor drains; it must call pdl_wait() before touching anything the predecessor writes.
+TCQ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+TCQ_HD void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---------------------------------------------------------------------------------------------------- host helpers
+#define TCQ_CHECK_LAUNCH()                                        \
+    do {                                                          \
+        cudaError_t e_ = cudaGetLastError();                      \
+        if (e_ != cudaSuccess) return TCQ_ERR_LAUNCH;             \
+    } while (0)
+
+static inline bool tcq_aligned(const void* p, size_t a) { return (((uintptr_t)p) & (a - 1)) == 0; }

@@ -1,0 +1,271 @@
+"""Launch helpers with the reference's operator interface, backed by the sm_100a C ABI.
+
+Mirrors deploy/tcq_kernels/kernels.py of the reference (ForeverBlue816/yanlongvla): the same function names, argument
+meaning and buffer layouts, so callers written against the reference work unchanged. Every call launches on
+torch.cuda.current_stream(), allocates nothing except the cached per-stream workspace of gemm_tcq, and therefore
+works inside torch.cuda.graph() captures. A non-zero status from the library raises TcqError.
+
+  pre      x (M, K) BF16/F16/F32 -> q (M, K) int8 and/or q4 (K/4, ld) int32, scale (M,)     (kernels.py:602-606)
+  post     acc (M, lda) I32 / F32 / BF16 columns col0.. -> y (M, N) BF16                    (kernels.py:612-615)
+  post3    q / k / v outputs of one accumulator row in one launch                            (kernels.py:618-621)
+  postg    up to three layers, one block per (token, layer), optional activation on layer 0  (kernels.py:624-628)
+  pre2     BF16(g * u) -> rotate -> INT8                                                      (kernels.py:631-633)
+  mid2     gated-MLP middle (GELU-tanh or SiLU)                                               (kernels.py:641-644)
+  mid1     plain-MLP middle                                                                   (kernels.py:647-650)
+  decode   trellis stream -> dense INT8 weights                                               (kernels.py:653-656)
+  gemm_w8  INT8-resident small-M product                                                      (kernels.py:662-668)
+  gemm_tcq trellis decode fused into the small-M product                                      (kernels.py:671-673)
+  pre_h, decode_bf16                                                                          (kernels.py:677-686)
+  rotate   the rotation op: fwht(x * s) and its inverse fwht(y) * s                          (tcq_format.py:44-55)
+  int_mm   exact INT8 GEMM on tcgen05 tensor cores, the reference's torch._int_mm(q, W.t())  (modules.py:86)
+  int8_gemm  the same with the per-token x per-channel scale epilogue (BF16 / FP32 out)      (tcq_format.py:135)
+"""
+import torch
+
+from ._lib import DT_BF16, DT_F16, DT_F32, DT_I32, TcqError, check, lib
+
+__all__ = ['pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
+           'gemm_tcq', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'device_error', 'gelu_table', 'silu_table', 'act_table',
+           'TcqError', 'LAUNCHES']
+
+_DT = {torch.bfloat16: DT_BF16, torch.float32: DT_F32, torch.float16: DT_F16, torch.int32: DT_I32}
+LAUNCHES = {}            # entry point -> number of calls (launch accounting for the benchmark)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _count(name):
+    LAUNCHES[name] = LAUNCHES.get(name, 0) + 1
+
+
+def _dt(t, allowed, what):
+    if t.dtype not in allowed:
+        raise TcqError(f'{what}: dtype {t.dtype} not supported (expected one of {allowed})')
+    return _DT[t.dtype]
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise TcqError('all tensors must be contiguous CUDA tensors')
+
+
+# ------------------------------------------------------------------------------------------------ activation tables
+_TABLES = {}
+
+
+def act_table(kind='gelu', device=None):
+    """BF16 activation of every BF16 bit pattern, computed by PyTorch on the device (65536 entries): the fused kernels
+    look the activation up, so they reproduce PyTorch's own result exactly (kernels.py:563-569). kind: 'gelu' (tanh
+    approximation, Gemma / SigLIP) or 'silu' (SwiGLU)."""
+    device = torch.device('cuda') if device is None else torch.device(device)
+    key = (kind, str(device))
+    if key not in _TABLES:
+        x = torch.arange(65536, dtype=torch.int32, device=device).to(torch.int16).view(torch.bfloat16)
+        if kind == 'gelu':
+            y = torch.nn.functional.gelu(x, approximate='tanh')
+        elif kind == 'silu':
+            y = torch.nn.functional.silu(x)
+        else:
+            raise ValueError(kind)
+        _TABLES[key] = y.contiguous()
+    return _TABLES[key]
+
+
+def gelu_table(device=None):
+    return act_table('gelu', device)
+
+
+def silu_table(device=None):
+    return act_table('silu', device)
+
+
+# ------------------------------------------------------------------------------------------------ rotation + quantizer
+def pre(x, su, q=None, q4=None, scale=None):
+    """x (M, K) BF16 / F16 / F32 contiguous -> q (M, K) int8 and / or q4 (K/4, ld) int32, scale (M,) FP32."""
+    _cuda(x, su, q, q4, scale)
+    M, K = x.shape
+    dt = _dt(x, (torch.bfloat16, torch.float16, torch.float32), 'pre')
+    check(lib.tcq_pre(_p(x), dt, _p(su), _p(q), _p(q4), _p(scale), M, K, 0 if q4 is None else q4.shape[1], _stream()), 'tcq_pre')
+    _count('pre')
+
+
+def pre2(g, u, su, q=None, q4=None, scale=None):
+    _cuda(g, u, su, q, q4, scale)
+    M, K = g.shape
+    check(lib.tcq_pre2(_p(g), _p(u), _p(su), _p(q), _p(q4), _p(scale), M, K, 0 if q4 is None else q4.shape[1], _stream()),
+          'tcq_pre2')
+    _count('pre2')
+
+
+def pre_h(x, su, h=None, hT=None):
+    _cuda(x, su, h, hT)
+    M, K = x.shape
+    dt = _dt(x, (torch.bfloat16, torch.float16, torch.float32), 'pre_h')
+    check(lib.tcq_pre_h(_p(x), dt, _p(su), _p(h), _p(hT), M, K, 0 if hT is None else hT.shape[1], _stream()), 'tcq_pre_h')
+    _count('pre_h')
+
+
+def _acc_dt(acc):
+    return _dt(acc, (torch.int32, torch.float32, torch.bfloat16), 'accumulator')
+
+
+def post(acc, s, rs, sv, bias, y, col0=0):
+    """acc (M, lda) int32 (scaled here by s, rs), FP32 (already scaled) or BF16 (scaled by rs); columns col0 .. col0 + N
+    -> y (M, N) BF16."""
+    _cuda(acc, s, rs, sv, bias, y)
+    M, N = y.shape
+    check(lib.tcq_post(_p(acc), _acc_dt(acc), _p(s), _p(rs), _p(sv), _p(bias), _p(y), M, N, acc.shape[1], col0, _stream()),
+          'tcq_post')
+    _count('post')
+
+
+def post3(acc, s, rs, sv, bias, ys):
+    """q / k / v in one launch: rs, sv, bias concatenated over the three layers; ys = three (M, N_i) BF16 outputs."""
+    _cuda(acc, s, rs, sv, bias, *ys)
+    M = ys[0].shape[0]
+    n = [y.shape[1] for y in ys]
+    check(lib.tcq_post3(_p(acc), _acc_dt(acc), _p(s), _p(rs), _p(sv), _p(bias), _p(ys[0]), _p(ys[1]), _p(ys[2]), M, n[0], n[1],
+                        n[2], acc.shape[1], _stream()), 'tcq_post3')
+    _count('post3')
+
+
+def postg(acc, s, rs, sv, bias, ys, gelu0=False, act='gelu'):
+    """Two or three layers sharing the accumulator row, one block per (token, layer); optional activation (GELU-tanh,
+    or SiLU with act='silu') on the first layer's output."""
+    _cuda(acc, s, rs, sv, bias, *ys)
+    M = ys[0].shape[0]
+    yy = list(ys) + [None] * (3 - len(ys))
+    n = [y.shape[1] for y in ys] + [0] * (3 - len(ys))
+    lut = act_table(act, acc.device) if gelu0 else None
+    check(lib.tcq_postg(_p(acc), _acc_dt(acc), _p(s), _p(rs), _p(sv), _p(bias), _p(lut), _p(yy[0]), _p(yy[1]), _p(yy[2]), M,
+                        n[0], n[1], n[2], acc.shape[1], int(bool(gelu0)), _stream()), 'tcq_postg')
+    _count('postg')
+
+
+def mid2_available(N):
+    """The fused gated-MLP middle holds N floats + N BF16 per token in shared memory: up to 16384 wide on sm_100a."""
+    return N <= 16384
+
+
+def mid2(acc, s, rs, sv, su, q=None, q4=None, scale=None, act='gelu'):
+    """Gated-MLP middle: acc (M, 2N) gate | up; rs, sv concatenated (2N); su = input signs of the down projection (N)."""
+    _cuda(acc, s, rs, sv, su, q, q4, scale)
+    M = acc.shape[0]
+    N = su.shape[0]
+    lut = act_table(act, acc.device)
+    check(lib.tcq_mid2(_p(acc), _acc_dt(acc), _p(s), _p(rs), _p(sv), _p(lut), _p(su), _p(q), _p(q4), _p(scale), M, N,
+                       acc.shape[1], 0 if q4 is None else q4.shape[1], _stream()), 'tcq_mid2')
+    _count('mid2')
+
+
+def mid1(acc, s, rs, sv, bias, su, q=None, q4=None, scale=None, act='gelu'):
+    """Plain-MLP middle: acc (M, N) of the first layer; su = input signs of the second layer."""
+    _cuda(acc, s, rs, sv, bias, su, q, q4, scale)
+    M, N = acc.shape
+    lut = act_table(act, acc.device)
+    check(lib.tcq_mid1(_p(acc), _acc_dt(acc), _p(s), _p(rs), _p(sv), _p(bias), _p(lut), _p(su), _p(q), _p(q4), _p(scale), M, N,
+                       N, 0 if q4 is None else q4.shape[1], _stream()), 'tcq_mid1')
+    _count('mid1')
+
+
+def rotate(x, signs, inverse=False, out_dtype=torch.float32, out=None):
+    """The rotation op: forward y = fwht(x * signs), inverse y = fwht(x) * signs, over the last dim (block Walsh over
+    its binary decomposition, FP32 arithmetic). x (..., D) BF16 / F16 / F32; y FP32 or BF16."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    M, D = x2.shape
+    y = torch.empty(M, D, dtype=out_dtype, device=x.device) if out is None else out.view(M, D)
+    _cuda(x2, signs, y)
+    dt = _dt(x2, (torch.bfloat16, torch.float16, torch.float32), 'rotate')
+    check(lib.tcq_rotate(_p(x2), dt, _p(signs), _p(y), _dt(y, (torch.float32, torch.bfloat16), 'rotate out'), M, D,
+                         int(bool(inverse)), _stream()), 'tcq_rotate')
+    _count('rotate')
+    return y.view(*shape)
+
+
+# ------------------------------------------------------------------------------------------------ trellis weights
+def decode(bits, t8, out):
+    """bits (m/16 * n/16, 32) int16/uint16 words, t8 (512, 2) int8 -> out (m, n) int8."""
+    _cuda(bits, t8, out)
+    m, n = out.shape
+    check(lib.tcq_decode(_p(bits), _p(t8), _p(out), m, n, _stream()), 'tcq_decode')
+    _count('decode')
+
+
+def decode_bf16(bits, tb, out):
+    _cuda(bits, tb, out)
+    m, n = out.shape
+    check(lib.tcq_decode_bf16(_p(bits), _p(tb), _p(out), m, n, _stream()), 'tcq_decode_bf16')
+    _count('decode_bf16')
+
+
+def gemm_w8(W, q4, s, rs, z):
+    """W (N, K) int8 resident, q4 (K/4, M) int32, z (M, N) FP32 = ((float)acc * s) * rs."""
+    _cuda(W, q4, s, rs, z)
+    N, K = W.shape
+    M = q4.shape[1]
+    check(lib.tcq_gemm_w8(_p(W), _p(q4), _p(s), _p(rs), _p(z), M, N, K, _stream()), 'tcq_gemm_w8')
+    _count('gemm_w8')
+
+
+_WS = {}
+
+
+def workspace(M, N, device):
+    """Zero-filled workspace of tcq_gemm_tcq for the current stream (kept zero by every call; grown on demand)."""
+    need = int(lib.tcq_gemm_tcq_workspace(M, N))
+    key = (str(device), _stream())
+    ws = _WS.get(key)
+    if ws is None or ws.numel() * 4 < need:
+        ws = torch.zeros(max(need // 4, 1 << 16), dtype=torch.int32, device=device)
+        _WS[key] = ws
+    return ws
+
+
+def gemm_tcq(bits, t8, q4, s, rs, z, K, bounds=(1 << 30, 1 << 30)):
+    """Fused trellis decode + product: bits (N/16 * K/16, 32) of up to three row-concatenated layers, t8 their tables
+    concatenated (1024 bytes each), bounds = tile-row boundaries between layers; z (M, N) FP32."""
+    _cuda(bits, t8, q4, s, rs, z)
+    M, N = z.shape
+    ws = workspace(M, N, z.device)
+    check(lib.tcq_gemm_tcq(_p(bits), _p(t8), _p(q4), _p(s), _p(rs), _p(z), M, N, K, int(bounds[0]), int(bounds[1]), _p(ws),
+                           ws.numel() * 4, _stream()), 'tcq_gemm_tcq')
+    _count('gemm_tcq')
+
+
+# ------------------------------------------------------------------------------------------------ W8A8 GEMM
+def int_mm(q, W, out=None):
+    """acc (M, N) int32 = q (M, K) int8 @ W (N, K) int8 ^T, exact (tcgen05 kind::i8); replaces torch._int_mm(q, W.t())."""
+    _cuda(q, W, out)
+    M, K = q.shape
+    N = W.shape[0]
+    out = torch.empty(M, N, dtype=torch.int32, device=q.device) if out is None else out
+    check(lib.tcq_int_mm(_p(q), _p(W), _p(out), M, N, K, _stream()), 'tcq_int_mm')
+    _count('int_mm')
+    return out
+
+
+def int8_gemm(q, W, s_tok, s_ch, out=None, out_dtype=torch.bfloat16):
+    """out (M, N) = ((float)(q @ W^T) * s_tok[:, None]) * s_ch[None, :] in BF16 or FP32, one launch."""
+    _cuda(q, W, s_tok, s_ch, out)
+    M, K = q.shape
+    N = W.shape[0]
+    out = torch.empty(M, N, dtype=out_dtype, device=q.device) if out is None else out
+    check(lib.tcq_int8_gemm(_p(q), _p(W), _p(s_tok), _p(s_ch), _p(out), _dt(out, (torch.bfloat16, torch.float32), 'int8_gemm out'),
+                            M, N, K, _stream()), 'tcq_int8_gemm')
+    _count('int8_gemm')
+    return out
+
+
+def device_error(reset=True):
+    """Error flags raised by the kernels' bounded pipeline waits (0 = none). Synchronizes the device."""
+    return int(lib.tcq_device_error(int(bool(reset))))
