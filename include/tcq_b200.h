@@ -128,6 +128,18 @@ size_t tcq_gemm_tcq_workspace(int M, int N);
 int tcq_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
                  int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. The fused decode-GEMV of tcq_gemm_tcq for callers that cannot allocate device
+ * memory (e.g. a real-time control loop that must not call cudaMalloc, or a plugin host that owns every device
+ * buffer): same arguments and bit-identical results, no workspace argument. Its scratch is a fixed ~2 MiB array inside
+ * this library (held on every GPU that loads it until exit); the first call on a device looks up its address (make
+ * that first call before any stream capture). Limits: 1 <= M <= 16, N <= 32768, M * N <= 524288, else TCQ_ERR_SHAPE.
+ * Calls share the array: calls that overlap on the GPU (different streams or threads) race. Allocates nothing. */
+int tcq_gemm_tcq_noalloc(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs,
+                         float* z, int M, int N, int K, int nb0, int nb1, void* stream);
+
+/* Largest M * N tcq_gemm_tcq_noalloc accepts. */
+size_t tcq_gemm_tcq_noalloc_max_elements(void);
+
 /* ------------------------------------------------------------------------------------------------ W8A8 INT8 GEMM
  * q (M, K) int8 row-major (tokens), W (N, K) int8 row-major (output channels); K a multiple of 16; q, W 16-byte
  * aligned. tcgen05 tensor cores (kind::i8), exact INT32 accumulation. */

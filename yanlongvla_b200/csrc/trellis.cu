@@ -15,6 +15,8 @@
 //   * the table is replicated once per lane (1024 keys x 32 lanes x 4 bytes = 128 KB), lane l reading bank l, so the
 //     random lookups of a warp never conflict;
 //   * decoded pairs are packed with one byte_perm per two pairs and consumed by dp4a in registers.
+#include <mutex>
+
 #include "tcq_common.cuh"
 
 namespace {
@@ -400,6 +402,32 @@ int launch_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const flo
     return TCQ_OK;
 }
 
+
+// ------------------------------------------------------------------------------------------------------ no-allocation variant
+// Scratch of tcq_gemm_tcq_noalloc: a fixed file-scope device array (every GPU that loads this library holds it, about
+// 2 MiB, until the process exits) instead of a caller-provided workspace. Host code must not pass the array's name to
+// a kernel (on the host it is only a stand-in symbol); the device address is looked up once per device with
+// cudaGetSymbolAddress, with that device current.
+constexpr int kNoAllocMaxMN = 16 * 32768;   // M * N limit (M <= 16, N <= 32768)
+constexpr int kNoAllocMaxN = 32768;
+static __device__ __align__(256) int g_gemv_scratch[kNoAllocMaxMN + kNoAllocMaxN / 16];
+
+constexpr int kMaxDevices = 64;
+int* g_scratch_addr[kMaxDevices];
+std::mutex g_scratch_mu;
+
+int scratch_for_current_device(int** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TCQ_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemv_scratch) != cudaSuccess || !p) return TCQ_ERR_DEVICE;
+        g_scratch_addr[dev] = reinterpret_cast<int*>(p);
+    }
+    *out = g_scratch_addr[dev];
+    return TCQ_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -466,4 +494,35 @@ int tcq_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const float*
     return launch_gemm_w8<16, 1>(W, q4, s, rs, z, M, N, K, st);
 }
 
+size_t tcq_gemm_tcq_noalloc_max_elements(void) { return (size_t)kNoAllocMaxMN; }
+
+// Fused decode-GEMV for callers that cannot allocate device memory: identical arguments and results to tcq_gemm_tcq,
+// without the workspace. Callers in this position are, for example, a robot's real-time control loop that must not
+// call cudaMalloc (it may synchronize the device and take an unbounded time in the middle of an action step), or a
+// host framework's plugin interface that owns every device buffer and hands the plugin only its inputs and outputs.
+// The stream-K scratch is the fixed array g_gemv_scratch; its device address is resolved on the first call on each
+// device (so that first call should come before any stream capture). Limits: 1 <= M <= 16, N <= 32768,
+// M * N <= 524288; larger shapes return TCQ_ERR_SHAPE. All calls share the one array per device: the used part is
+// cleared (cudaMemsetAsync, no allocation) on the caller's stream before the kernel, and calls that overlap on the GPU
+// (other streams, other host threads) race on it. Allocates nothing: no cudaMalloc / cudaFree / library allocation.
+int tcq_gemm_tcq_noalloc(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
+                         int M, int N, int K, int nb0, int nb1, void* stream) {
+    if (!bits || !t8 || !q4 || !s || !rs || !z) return TCQ_ERR_ARG;
+    if (M < 1 || M > 16 || N <= 0 || K <= 0 || (N & 15) || (K & 15)) return TCQ_ERR_SHAPE;
+    if (N > kNoAllocMaxN || (long long)M * N > kNoAllocMaxMN) return TCQ_ERR_SHAPE;
+    if (!tcq_aligned(bits, 16) || !tcq_aligned(q4, 4) || !tcq_aligned(t8, 16)) return TCQ_ERR_ALIGN;
+    if (nb0 < 0 || nb1 < 0) return TCQ_ERR_ARG;
+    int* ws = nullptr;
+    const int e = scratch_for_current_device(&ws);
+    if (e) return e;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemsetAsync(ws, 0, tcq_gemm_tcq_workspace(M, N), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
+    if (M == 1) return launch_gemm_tcq<1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M == 2) return launch_gemm_tcq<2>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 4) return launch_gemm_tcq<4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 8) return launch_gemm_tcq<8>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return launch_gemm_tcq<16>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+}
+
 }  // extern "C"
+
