@@ -17,106 +17,13 @@
 //   * decoded pairs are packed with one byte_perm per two pairs and consumed by dp4a in registers.
 #include <mutex>
 
-#include "tcq_common.cuh"
+#include "trellis_common.cuh"
 
 namespace {
 
-constexpr int kTabBytes = 1024 * 32 * 4;   // per-lane replicated decode table
+using namespace tcq;
+
 constexpr int kThreads = 512;
-
-// Table entry for key k (bits 6..15 of x): pair index k & 511, sign k >> 9.
-// INT8 entry: byte 0 = (sign ? -v0 : v0), byte 1 = v1. The 1 KB source table is staged through shared memory with one
-// 16-byte load per thread (one memory round trip), then the 128 KB replicated table is written with consecutive
-// 16-byte stores (lanes of a warp cover 512 contiguous bytes: no bank conflicts).
-__device__ __forceinline__ void stage_pairs(u16* pairs, const void* __restrict__ src) {
-    if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(src) + threadIdx.x);
-    __syncthreads();
-}
-
-__device__ __forceinline__ void build_table_i8(u32* tab, u16* pairs, const i8* __restrict__ t8) {
-    stage_pairs(pairs, t8);
-    uint4* t4 = reinterpret_cast<uint4*>(tab);
-    for (int i = threadIdx.x; i < 1024 * 8; i += blockDim.x) {
-        const int k = i >> 3;
-        const u32 pr = pairs[k & 511];
-        const u32 v0 = (k >> 9) ? ((0u - pr) & 0xffu) : (pr & 0xffu);
-        const u32 e = v0 | (pr & 0xff00u);
-        t4[i] = make_uint4(e, e, e, e);
-    }
-}
-
-// BF16 entry: low half = BF16(v0) with the sign bit flipped for sign keys, high half = BF16(v1) (kernels.py:320-337).
-// pairs: 512 staged (v0, v1) BF16 pairs (2 KB, staged with one 16-byte load by each of 128 threads).
-__device__ __forceinline__ void build_table_bf16(u32* tab, u32* pairs, const u16* __restrict__ tb) {
-    if (threadIdx.x < 128) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(tb) + threadIdx.x);
-    __syncthreads();
-    uint4* t4 = reinterpret_cast<uint4*>(tab);
-    for (int i = threadIdx.x; i < 1024 * 8; i += blockDim.x) {
-        const int k = i >> 3;
-        const u32 e = pairs[k & 511] ^ ((u32)(k >> 9) << 15);
-        t4[i] = make_uint4(e, e, e, e);
-    }
-}
-
-// Table lookup of this lane's copy: byte offset (key * 128) | (4 * lane) from the shared table `tab` (the key offset
-// has bits 7..16, the lane offset bits 2..6, so one OR joins them; the constant shared base is added by the compiler).
-__device__ __forceinline__ u32 lut(const u32* tab, u32 lane4, u32 off) {
-    return *reinterpret_cast<const u32*>(reinterpret_cast<const char*>(tab) + (off | lane4));
-}
-
-// Byte offset key * 128 of the state in the upper half of F: v = F >> 16 taken as the high word of F * 2^16 (multiply
-// pipe), 2x = v * 2v + 2v, bits 7..16 of 2x = bits 6..15 of x = key.
-__device__ __forceinline__ u32 off_hi(u32 F) {
-    const u32 v = __umulhi(F, 65536u), u = v * 2u;
-    return (v * u + u) & 0x1FF80u;
-}
-// Byte offset of the state in the lower half of F (bits above 16 are junk and drop out of bits 7..16 of 2x).
-__device__ __forceinline__ u32 off_lo(u32 F) {
-    const u32 u = F * 2u;
-    return (F * u + u) & 0x1FF80u;
-}
-
-// The 8 table entries of one tile row. A = (w[2r] << 16) | w[2r+1], B = (w[2r+2] << 16) | w[2r+3] (words mod 32):
-// F_p = bits [4p, 4p + 32) of the row's window, so its upper half is state p and its lower half state p + 4.
-__device__ __forceinline__ void row_entries(u32 A, u32 B, const u32* tab, u32 lane4, u32 (&e)[8]) {
-    const u32 F1 = __funnelshift_l(B, A, 4), F2 = __funnelshift_l(B, A, 8), F3 = __funnelshift_l(B, A, 12);
-    e[0] = lut(tab, lane4, off_hi(A));
-    e[1] = lut(tab, lane4, off_hi(F1));
-    e[2] = lut(tab, lane4, off_hi(F2));
-    e[3] = lut(tab, lane4, off_hi(F3));
-    e[4] = lut(tab, lane4, off_lo(A));
-    e[5] = lut(tab, lane4, off_lo(F1));
-    e[6] = lut(tab, lane4, off_lo(F2));
-    e[7] = lut(tab, lane4, off_lo(F3));
-}
-
-// INT8 weights of one tile row as 4 little-endian words (columns 4j .. 4j+3 in word j).
-__device__ __forceinline__ void row_words_i8(u32 A, u32 B, const u32* tab, u32 lane4, u32 (&w)[4]) {
-    u32 e[8];
-    row_entries(A, B, tab, lane4, e);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = __byte_perm(e[2 * j], e[2 * j + 1], 0x5410);
-}
-
-// Tile row r's A word from the tile's 32-bit words: swap the two uint16 halves (memory is little endian, the stream
-// is MSB first).
-__device__ __forceinline__ u32 rowA(u32 word) { return __byte_perm(word, 0, 0x1032); }
-
-// Words rg*RPT .. rg*RPT+RPT (mod 16) of a tile: row a of the lane's row group is (W[a], W[a + 1]).
-template <int RPT>
-__device__ __forceinline__ void load_tile_rows(const u16* __restrict__ bits, size_t tile, int rg, u32 (&W)[RPT + 1]) {
-    const u32* tw = reinterpret_cast<const u32*>(bits + tile * 32);
-    if (RPT == 16) {
-        const uint4* tp = reinterpret_cast<const uint4*>(tw);
-        const uint4 a0 = ldg_stream_v4(tp), a1 = ldg_stream_v4(tp + 1), a2 = ldg_stream_v4(tp + 2), a3 = ldg_stream_v4(tp + 3);
-        const u32 all[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
-#pragma unroll
-        for (int a = 0; a <= RPT; ++a) W[a] = all[a & 15];
-    } else {
-#pragma unroll
-        for (int a = 0; a <= RPT; ++a) W[a] = __ldg(tw + ((rg * RPT + a) & 15));
-    }
-}
 
 // ------------------------------------------------------------------------------------------------------ dense decode
 // One thread per tile: its 64 bytes arrive with four 16-byte loads (the next tile of the thread is fetched while this
@@ -194,21 +101,20 @@ struct Parts {
 
 constexpr int kMaxRows = 24;    // tile rows one CTA may touch (the launcher bounds the units per CTA accordingly)
 
-// Sum RPT x MT accumulators over the lanes that hold the same row group (lanes differing in bits >= log2(LT)) by
-// recursive halving: each exchange step sends half of the remaining values and keeps the other half, so 16 values
-// need 8 + 4 + 2 + 1 shuffles instead of 16 per step. On return lane l holds KEEP values; value i is the flattened
-// index out_index(l, i) = a * MT + m of its row group's accumulator array.
-template <int MT>
+// Sum V = RPT x MT accumulators over the lanes that hold the same row group (lanes differing in bits >= log2(LT)) by
+// recursive halving: each exchange step sends half of the remaining values and keeps the other half (16 values over
+// 32 lanes: 8 + 4 + 2 + 1 + 1 shuffles instead of 80). On return lane l holds KEEP values; value i is element
+// out_index(l, i) (= a * MT + m) of its row group's accumulator array; lanes with writer(l) hold distinct sums.
+template <int V, int LT>
 struct LaneReduce {
-    static constexpr int LT = MT;
-    static constexpr int P = 32 / LT;                       // lanes sharing a row group
-    static constexpr int LOGP = P == 32 ? 5 : P == 16 ? 4 : P == 8 ? 3 : P == 4 ? 2 : 1;
-    static constexpr int STEPS = LOGP < 4 ? LOGP : 4;       // halving steps (16 values)
-    static constexpr int KEEP = 16 >> STEPS;
-    __device__ __forceinline__ static void run(int (&v)[16], int lane) {
+    static constexpr int LOGV = V == 16 ? 4 : V == 8 ? 3 : V == 4 ? 2 : V == 2 ? 1 : 0;
+    static constexpr int LOGP = LT == 1 ? 5 : LT == 2 ? 4 : LT == 4 ? 3 : LT == 8 ? 2 : 1;
+    static constexpr int STEPS = LOGV < LOGP ? LOGV : LOGP;
+    static constexpr int KEEP = V >> STEPS;
+    __device__ __forceinline__ static void run(int (&v)[V], int lane) {
 #pragma unroll
         for (int j = 0; j < STEPS; ++j) {
-            const int o = 16 >> j, half = 8 >> j;
+            const int o = 16 >> j, half = V >> (j + 1);
             const bool up = (lane & o) != 0;
 #pragma unroll
             for (int i = 0; i < half; ++i) {
@@ -217,17 +123,24 @@ struct LaneReduce {
                 v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
         }
-        if (LOGP == 5) v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+#pragma unroll
+        for (int j = STEPS; j < LOGP; ++j)
+#pragma unroll
+            for (int i = 0; i < KEEP; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16 >> j);
     }
     __device__ __forceinline__ static int out_index(int lane, int i) {
         int idx = i;
 #pragma unroll
         for (int j = 0; j < STEPS; ++j)
-            if (lane & (16 >> j)) idx += 8 >> j;
+            if (lane & (16 >> j)) idx += V >> (j + 1);
         return idx;
     }
-    // lanes that write: all, except the duplicate odd lanes of the 32-lane case
-    __device__ __forceinline__ static bool writer(int lane) { return LOGP != 5 || (lane & 1) == 0; }
+    __device__ __forceinline__ static bool writer(int lane) {
+        int mask = 0;
+#pragma unroll
+        for (int j = STEPS; j < LOGP; ++j) mask |= 16 >> j;
+        return (lane & mask) == 0;
+    }
 };
 
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
@@ -236,16 +149,16 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
     return old;
 }
 
-template <int MT>
+template <int MT, int LT>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* __restrict__ q4, const float* __restrict__ s,
            const float* __restrict__ rs, float* __restrict__ z, int M, int N, int K, Parts parts, int* __restrict__ ws_acc,
            int* __restrict__ ws_cnt, int act_vec) {
-    constexpr int LT = MT;          // lanes per tile
-    constexpr int RPT = 16 / MT;    // tile rows per lane
+    constexpr int RPT = 16 / LT;    // tile rows per lane (LT lanes share a tile)
     constexpr int TPU = 32 / LT;    // tiles per unit
     constexpr int RV = 16 * MT;     // partial sums per tile row
-    using Red = LaneReduce<MT>;
+    constexpr int V = RPT * MT;     // accumulators per lane
+    using Red = LaneReduce<V, LT>;
     extern __shared__ __align__(128) u32 tab[];
     __shared__ __align__(16) u16 pairs[512];
     __shared__ int racc[kMaxRows * RV];
@@ -288,9 +201,9 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
             const int rn = un / S, tcn = (un - rn * S) * TPU + tin;
             if (tcn < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rn) * tiles + tcn, rg, Wn);
         }
-        int acc[16];
+        int acc[V];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0;
+        for (int i = 0; i < V; ++i) acc[i] = 0;
         if (tc < tiles) {
             int act[4][MT];
             const int* qa = q4 + (size_t)4 * tc * M;
@@ -480,12 +393,12 @@ int decode_grid(int m, int n) {
     return (int)(grid < num_sms() ? grid : num_sms());
 }
 
-template <int MT>
+template <int MT, int LT>
 int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
                     int M, int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
-    auto kern = k_gemm_tcq<MT>;
+    auto kern = k_gemm_tcq<MT, LT>;
     if (set_smem(kern, kTabBytes)) return TCQ_ERR_LAUNCH;
-    const int TPU = 32 / MT, tiles = K >> 4, S = (tiles + TPU - 1) / TPU, R = N >> 4;
+    const int TPU = 32 / LT, tiles = K >> 4, S = (tiles + TPU - 1) / TPU, R = N >> 4;
     Parts p{};
     int bounds[4] = {0, nb0 < R ? nb0 : R, nb1 < R ? nb1 : R, R};
     if (bounds[2] < bounds[1]) bounds[2] = bounds[1];
@@ -500,6 +413,10 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
         if (rows[l] <= 0) continue;
         const long long Ul = (long long)rows[l] * S;
         long long g = (sms * Ul + U - 1) / U;
+        // Whole tile rows per CTA need no cross-CTA finish; take that split when its imbalance against the even
+        // stream-K split is at most 20 %.
+        const long long rows_per = (rows[l] + g - 1) / g;
+        if (rows_per * g * 5 <= (long long)rows[l] * 6 && rows_per <= kMaxRows) g = (rows[l] + rows_per - 1) / rows_per;
         const long long gmin = (Ul + (long long)(kMaxRows - 2) * S - 1) / ((long long)(kMaxRows - 2) * S);   // rows per CTA <= kMaxRows
         if (g < gmin) g = gmin;
         if (g < 1) g = 1;
@@ -530,6 +447,20 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
                            M, N, K, p, ws_acc, ws_cnt, act_vec) != cudaSuccess)
         return TCQ_ERR_LAUNCH;
     return TCQ_OK;
+}
+
+// Lanes per tile: for M = 1 on layers with fewer tiles than threads on the machine, four lanes split a tile's rows
+// (a warp covers 8 tiles, every SM gets many small units and the load latency hides); on larger layers one lane per
+// tile (fewest instructions per weight). M <= 4: 4 lanes; larger M: one lane per token slot (MT lanes).
+int dispatch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z, int M,
+                      int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
+    const long long tiles = (long long)(N >> 4) * (K >> 4);
+    if (M == 1 && tiles >= (long long)num_sms() * kThreads) return launch_gemm_tcq<1, 1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M == 1) return launch_gemm_tcq<1, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M == 2) return launch_gemm_tcq<2, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 4) return launch_gemm_tcq<4, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 8) return launch_gemm_tcq<8, 8>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return launch_gemm_tcq<16, 16>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }
 
 template <int MT, int RPW>
@@ -615,11 +546,7 @@ int tcq_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, cons
     if (nb0 < 0 || nb1 < 0) return TCQ_ERR_ARG;
     int* ws = reinterpret_cast<int*>(workspace);
     cudaStream_t st = (cudaStream_t)stream;
-    if (M == 1) return launch_gemm_tcq<1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M == 2) return launch_gemm_tcq<2>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 4) return launch_gemm_tcq<4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 8) return launch_gemm_tcq<8>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    return launch_gemm_tcq<16>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return dispatch_gemm_tcq(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }
 
 int tcq_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const float* rs, float* z, int M, int N, int K,
@@ -659,11 +586,7 @@ int tcq_gemm_tcq_noalloc(const uint16_t* bits, const int8_t* t8, const int32_t* 
     if (e) return e;
     cudaStream_t st = (cudaStream_t)stream;
     if (cudaMemsetAsync(ws, 0, tcq_gemm_tcq_workspace(M, N), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
-    if (M == 1) return launch_gemm_tcq<1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M == 2) return launch_gemm_tcq<2>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 4) return launch_gemm_tcq<4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 8) return launch_gemm_tcq<8>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    return launch_gemm_tcq<16>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return dispatch_gemm_tcq(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }
 
 }  // extern "C"
