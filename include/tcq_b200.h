@@ -153,6 +153,17 @@ int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int
 int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype,
                   int M, int N, int K, void* stream);
 
+/* Workspace of tcq_gemm_tcq_tc in bytes for (M, N); same zero-filled contract as tcq_gemm_tcq_workspace. */
+size_t tcq_gemm_tcq_tc_workspace(int M, int N);
+
+/* Tensor-core form of kernels.gemm_tcq (kernels.py:671-673) for 1 <= M <= 256 tokens, and the on-the-fly prefill
+ * product of the reference (k_decode + torch._int_mm, modules.py:81-86) without the dense INT8 weights: the trellis
+ * stream is decoded straight into shared memory and consumed by tcgen05.mma.kind::i8. q (M, K) int8 row-major
+ * (tcq_pre's q output), z (M, N) float32 = ((float)acc * s[t]) * rs[n], bit-exact. Layer bounds nb0 / nb1 (tile rows)
+ * must be multiples of 8 (128 output rows) or >= N/16. workspace: tcq_gemm_tcq_tc_workspace(M, N) bytes. */
+int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z,
+                    int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device error flags raised by bounded waits inside the kernels (1 = a pipeline wait expired and the kernel stopped
  * early). Synchronizes the current device. reset != 0 clears the flags. Returns -1 if the flags cannot be read. */
 int tcq_device_error(int reset);

@@ -85,3 +85,36 @@ def test_int_mm_repeated_and_graph(K):
     g.replay()
     torch.cuda.synchronize()
     assert np.array_equal(n(out), ref)
+
+
+@pytest.mark.parametrize('M', [1, 3, 17, 33, 64, 100, 160, 256])
+@pytest.mark.parametrize('N,Kd', [(1536, 1536), (256, 4304), (2048, 2048)])
+def test_gemm_tcq_tc_exact(K, M, N, Kd):
+    """Trellis decode fused into the tcgen05 product: bit-exact z against the oracle, twice (workspace left clean)."""
+    from gpu_util import DevLayer
+    L = DevLayer(f'tc{N}x{Kd}', N, Kd, False)
+    x = cases.activations(f'tc{N}x{Kd}', M, Kd, 'bf16')
+    q, s = O.pre(x, 'bf16', L.ref.su)
+    zr = O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs)
+    z = torch.empty(M, N, dtype=torch.float32, device='cuda')
+    for _ in range(2):
+        z.fill_(float('nan'))
+        K.gemm_tcq_tc(L.bits, L.t8, t(q), t(s), L.rs, z, Kd)
+        got = n(z)
+        assert np.array_equal(got, zr), f'{int((got != zr).sum())} of {zr.size} differ'
+
+
+def test_gemm_tcq_tc_three_layers(K):
+    """q / k / v (2048 + 512 + 512 rows) with their own tables, 160 tokens (the policy's LLM prefix)."""
+    from gpu_util import DevLayer
+    Ls = [DevLayer(f'tcqkv{i}', m, 2048, False) for i, m in enumerate((2048, 512, 512))]
+    M = 160
+    x = cases.activations('tcqkv', M, 2048, 'bf16')
+    q, s = O.pre(x, 'bf16', Ls[0].ref.su)
+    bits = torch.cat([L.bits for L in Ls]).contiguous()
+    t8 = torch.cat([L.t8.reshape(-1) for L in Ls]).contiguous()
+    rs = torch.cat([L.rs for L in Ls]).contiguous()
+    z = torch.empty(M, 3072, dtype=torch.float32, device='cuda')
+    K.gemm_tcq_tc(bits, t8, t(q), t(s), rs, z, 2048, bounds=(128, 160))
+    zr = np.concatenate([O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs) for L in Ls], 1)
+    assert np.array_equal(n(z), zr)

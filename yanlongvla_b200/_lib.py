@@ -34,11 +34,13 @@ SIGNATURES = {
     'tcq_gemm_tcq': [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P],
     'tcq_gemm_tcq_noalloc': [P, P, P, P, P, P, I, I, I, I, I, P],
     'tcq_gemm_tcq_noalloc_max_elements': [],
+    'tcq_gemm_tcq_tc_workspace': [I, I],
+    'tcq_gemm_tcq_tc': [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P],
     'tcq_int_mm': [P, P, P, I, I, I, P],
     'tcq_int8_gemm': [P, P, P, P, P, I, I, I, I, P],
     'tcq_device_error': [I],
 }
-RESTYPES = {'tcq_status_string': ctypes.c_char_p, 'tcq_gemm_tcq_workspace': SZ, 'tcq_gemm_tcq_noalloc_max_elements': SZ}
+RESTYPES = {'tcq_status_string': ctypes.c_char_p, 'tcq_gemm_tcq_workspace': SZ, 'tcq_gemm_tcq_tc_workspace': SZ, 'tcq_gemm_tcq_noalloc_max_elements': SZ}
 
 
 def _load():

@@ -15,7 +15,7 @@
 // for its copies and MMAs in flight, frees TMEM and returns; tcq_device_error() reports the flag.
 #include <cuda.h>
 
-#include "tcq_common.cuh"
+#include "trellis_common.cuh"
 
 __device__ int g_tcq_device_error;
 
@@ -271,6 +271,201 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
     }
 }
 
+
+// ------------------------------------------------------------------------------------------------ fused decode-GEMM
+// z (M, N) FP32 = ((float)(q W^T) * s[t]) * rs[n] with W decoded from the trellis stream straight into shared memory:
+// the decoded weights never leave the SM. One CTA = one 128-channel tile (8 tile rows) x one K range; per 128-byte K
+// stage, 16 decoder warps write the 128 x 128 INT8 A tile in the 128B-swizzled K-major UMMA layout (512 threads x 2
+// tile rows), TMA brings the BN x 128 activation tile, one thread issues four tcgen05.mma.kind::i8 (M = 128, N = BN,
+// K = 32) into TMEM. Epilogue (decoder warps 2..5, one TMEM lane quarter each): scale and store z, or, when K is split
+// over several CTAs, add INT32 partials into the workspace; the CTA that completes a channel tile writes z and zeroes
+// the workspace again (the same exact finish as the small-M kernel).
+constexpr int kTcDecWarps = 16;
+constexpr int kTcThreads = 64 + 32 * kTcDecWarps;
+
+struct TcParts {
+    int ct;         // channel tiles
+    int ks;         // K splits per channel tile
+    int kb;         // 128-byte K stages
+    int nb0, nb1;   // layer bounds in tile rows (multiples of 8)
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1)
+k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ bits, const i8* __restrict__ t8,
+              const float* __restrict__ s_tok, const float* __restrict__ rs, float* __restrict__ z, int M, int N, int K,
+              TcParts P, int* __restrict__ ws_acc, int* __restrict__ ws_cnt) {
+    constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
+    constexpr u32 TMEM_COLS = BN < 32 ? 32 : BN;
+    constexpr u32 IDESC = idesc_i8(BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    u32* tab = reinterpret_cast<u32*>(smem);                         // 128 KB decode table
+    uint8_t* sA = smem + tcq::kTabBytes;
+    uint8_t* sB = sA + STAGES * A_BYTES;
+    u16* pairs = reinterpret_cast<u16*>(sB + STAGES * B_BYTES);       // 1 KB staging of t8 (1024-byte aligned)
+    u64* bars = reinterpret_cast<u64*>(sB + STAGES * B_BYTES + 1024);
+    u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * STAGES + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+    const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull = smem_u32(bars + 2 * STAGES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ct = blockIdx.x / P.ks, ksi = blockIdx.x % P.ks;
+    const int kb0 = (int)((long long)P.kb * ksi / P.ks), kb1 = (int)((long long)P.kb * (ksi + 1) / P.ks);
+    const int tr0 = ct * 8, tiles_k = K >> 4, tiles_n = N >> 4;
+    const int slot = (tr0 >= P.nb0) + (tr0 >= P.nb1);
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < STAGES; ++st) {
+            mbar_init(full0 + 8 * st, 32 * kTcDecWarps + 1);
+            mbar_init(empty0 + 8 * st, 1);
+        }
+        mbar_init(tfull, 1);
+        *abort_flag = 0;
+        *last_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    pdl_launch_dependents();
+    tcq::build_table_i8(tab, pairs, t8 + 1024 * slot);               // weights only: before the dependency wait
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const u32 tmem = *tmem_slot;
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmQ) : "memory");
+            int st = 0;
+            u32 ph = 0;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(empty0 + 8 * st, ph ^ 1, abort_flag)) break;
+                mbar_expect_tx(full0 + 8 * st, B_BYTES);
+                tma_load_2d(smem_u32(sB + st * B_BYTES), &tmQ, full0 + 8 * st, kb * BK, 0);
+                if (++st == STAGES) { st = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int st = 0;
+            u32 ph = 0;
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(full0 + 8 * st, ph, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const u32 aaddr = smem_u32(sA + st * A_BYTES), baddr = smem_u32(sB + st * B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / 32; ++k)
+                    mma_i8(tmem, sw128_desc(aaddr + 32 * k), sw128_desc(baddr + 32 * k), IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+                mma_commit(empty0 + 8 * st);
+                if (++st == STAGES) { st = 0; ph ^= 1; }
+            }
+            (void)ok;
+            mma_commit(tfull);   // also on an early stop: it arrives once every MMA issued so far has finished
+        }
+    } else {
+        // ---- decoders: thread d -> tile (i, j) = (d >> 6, (d >> 3) & 7) of the stage, tile rows 2g, 2g + 1 (g = d & 7)
+        const int d = threadIdx.x - 64;
+        const int i = d >> 6, j = (d >> 3) & 7, g = d & 7;
+        const u32 lane4 = 4u * lane;
+        const bool row_ok = tr0 + i < tiles_n;
+        int st = 0;
+        u32 ph = 0;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            const int tc = kb * 8 + j;
+            u32 w0 = 0, w1 = 0, w2 = 0;
+            const bool ok = row_ok && tc < tiles_k;
+            if (ok) {
+                const u32* tw = reinterpret_cast<const u32*>(bits + ((size_t)(tr0 + i) * tiles_k + tc) * 32);
+                w0 = __ldg(tw + 2 * g);
+                w1 = __ldg(tw + 2 * g + 1);
+                w2 = __ldg(tw + ((2 * g + 2) & 15));
+            }
+            if (!mbar_wait(empty0 + 8 * st, ph ^ 1, abort_flag)) break;
+            uint8_t* a = sA + st * A_BYTES;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = 16 * i + 2 * g + h;
+                u32 wd[4] = {0, 0, 0, 0};
+                if (ok) tcq::row_words_i8(tcq::rowA(h ? w1 : w0), tcq::rowA(h ? w2 : w1), tab, lane4, wd);
+                *reinterpret_cast<uint4*>(a + row * 128 + ((j ^ (row & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor-core reads
+            mbar_arrive(full0 + 8 * st);
+            if (++st == STAGES) { st = 0; ph ^= 1; }
+        }
+        // ---- epilogue: decoder warps 2..5 (warp index 4..7), one TMEM lane quarter each
+        if (warp >= 4 && warp < 8) {
+            const int q = warp & 3;
+            const int ch = ct * BM + 32 * q + lane;
+            const bool chok = ch < N;
+            if (mbar_wait(tfull, 0, abort_flag)) {
+                tc_fence_after();
+                const float r = chok ? rs[ch] : 0.f;
+#pragma unroll 1
+                for (int c = 0; c < (BN + 31) / 32; ++c) {
+                    u32 v[32];
+                    tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(32 * c), v);
+                    if (chok) {
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) {
+                            const int tok = 32 * c + jj;
+                            if (tok < M) {
+                                const size_t o = (size_t)tok * N + ch;
+                                if (P.ks == 1) z[o] = ((float)(int)v[jj] * s_tok[tok]) * r;
+                                else atomicAdd(ws_acc + o, (int)v[jj]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // Split K: every CTA has added its partials; the one whose arrival completes the channel tile finishes it. The
+    // decision sits between two CTA-wide barriers that every thread reaches on every path.
+    __syncthreads();
+    if (P.ks > 1 && threadIdx.x == 0) {
+        int done = 0;
+        if (!*abort_flag) {
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ws_cnt + ct) : "memory");
+            done = old + 1 == P.ks;
+            if (done) ws_cnt[ct] = 0;
+        }
+        *last_flag = done;
+    }
+    __syncthreads();
+    if (P.ks > 1 && *last_flag && warp >= 4 && warp < 8) {
+        const int ch = ct * BM + 32 * (warp & 3) + lane;
+        if (ch < N) {
+            const float r = rs[ch];
+            for (int tok = 0; tok < M; ++tok) {
+                const size_t o = (size_t)tok * N + ch;
+                const int vv = atomicExch(ws_acc + o, 0);
+                z[o] = ((float)vv * s_tok[tok]) * r;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        if (*abort_flag && lane == 0) {
+            // MMAs already issued must finish before TMEM is freed: wait (bounded) for the final commit.
+            volatile int never = 0;
+            mbar_wait(tfull, 0, &never, 100000000ull);
+        }
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ host side
 int g_sms_i8 = 0;
 int sms() {
@@ -345,6 +540,38 @@ int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, co
     return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
 }
 
+
+template <int BN, int STAGES>
+int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z, int M, int N,
+              int K, int nb0, int nb1, int* ws, cudaStream_t st) {
+    CUtensorMap tmQ;
+    if (!make_map(&tmQ, q, M, K, BN)) return TCQ_ERR_ARG;
+    auto kern = k_gemm_tcq_tc<BN, STAGES>;
+    const int smem = 1024 + tcq::kTabBytes + STAGES * (BM + BN) * BK + (2 * STAGES + 1) * 8 + 16 + 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
+    TcParts P;
+    P.ct = (N + BM - 1) / BM;
+    P.kb = (K + BK - 1) / BK;
+    int ks = sms() / P.ct;
+    if (ks < 1) ks = 1;
+    if (ks > P.kb) ks = P.kb;
+    P.ks = ks;
+    P.nb0 = nb0;
+    P.nb1 = nb1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P.ct * P.ks);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmQ, reinterpret_cast<const u16*>(bits), reinterpret_cast<const i8*>(t8), s, rs, z, M, N,
+                              K, P, ws, ws + (size_t)M * N) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+}
+
 int check_args(const int8_t* q, const int8_t* W, const void* out, int M, int N, int K) {
     if (!q || !W || !out) return TCQ_ERR_ARG;
     if (M <= 0 || N <= 0 || K <= 0 || (K & 15)) return TCQ_ERR_SHAPE;
@@ -370,6 +597,28 @@ int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const fl
     if (out_dtype == TCQ_DT_BF16) return dispatch<OUT_BF16>(q, W, out, s_tok, s_ch, M, N, K, (cudaStream_t)stream);
     if (out_dtype == TCQ_DT_F32) return dispatch<OUT_F32>(q, W, out, s_tok, s_ch, M, N, K, (cudaStream_t)stream);
     return TCQ_ERR_DTYPE;
+}
+
+
+size_t tcq_gemm_tcq_tc_workspace(int M, int N) {
+    if (M <= 0 || N <= 0) return 0;
+    return ((size_t)M * N + (size_t)((N + BM - 1) / BM)) * sizeof(int);
+}
+
+int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z, int M, int N,
+                    int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bits || !t8 || !q || !s || !rs || !z) return TCQ_ERR_ARG;
+    if (M < 1 || M > 256 || N <= 0 || K <= 0 || (N & 15) || (K & 15)) return TCQ_ERR_SHAPE;
+    const int R = N >> 4;
+    if ((nb0 < R && (nb0 & 7)) || (nb1 < R && (nb1 & 7)) || nb0 < 0 || nb1 < 0) return TCQ_ERR_SHAPE;   // layers on 128-row tiles
+    if (!tcq_aligned(bits, 16) || !tcq_aligned(q, 16) || !tcq_aligned(t8, 16)) return TCQ_ERR_ALIGN;
+    if (!workspace || workspace_bytes < tcq_gemm_tcq_tc_workspace(M, N)) return TCQ_ERR_WORKSPACE;
+    int* ws = reinterpret_cast<int*>(workspace);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M <= 32) return launch_tc<32, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 64) return launch_tc<64, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 128) return launch_tc<128, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return launch_tc<256, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }
 
 int tcq_device_error(int reset) {

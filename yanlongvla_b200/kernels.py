@@ -25,7 +25,7 @@ import torch
 from ._lib import DT_BF16, DT_F16, DT_F32, DT_I32, TcqError, check, lib
 
 __all__ = ['pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
-           'gemm_tcq', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'device_error', 'gelu_table', 'silu_table', 'act_table',
+           'gemm_tcq', 'gemm_tcq_tc', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'device_error', 'gelu_table', 'silu_table', 'act_table',
            'TcqError', 'LAUNCHES']
 
 _DT = {torch.bfloat16: DT_BF16, torch.float32: DT_F32, torch.float16: DT_F16, torch.int32: DT_I32}
@@ -221,8 +221,9 @@ _WS = {}
 
 
 def workspace(M, N, device):
-    """Zero-filled workspace of tcq_gemm_tcq for the current stream (kept zero by every call; grown on demand)."""
-    need = int(lib.tcq_gemm_tcq_workspace(M, N))
+    """Zero-filled workspace of tcq_gemm_tcq / tcq_gemm_tcq_tc for the current stream (every call leaves it zero;
+    grown on demand)."""
+    need = max(int(lib.tcq_gemm_tcq_workspace(M, N)), int(lib.tcq_gemm_tcq_tc_workspace(M, N)))
     key = (str(device), _stream())
     ws = _WS.get(key)
     if ws is None or ws.numel() * 4 < need:
@@ -269,3 +270,15 @@ def int8_gemm(q, W, s_tok, s_ch, out=None, out_dtype=torch.bfloat16):
 def device_error(reset=True):
     """Error flags raised by the kernels' bounded pipeline waits (0 = none). Synchronizes the device."""
     return int(lib.tcq_device_error(int(bool(reset))))
+
+
+def gemm_tcq_tc(bits, t8, q, s, rs, z, K, bounds=(1 << 30, 1 << 30)):
+    """Tensor-core fused decode-GEMM: q (M, K) int8 row-major (pre's q output), 1 <= M <= 256; z (M, N) FP32 =
+    ((float)acc * s) * rs, the weights decoded from the trellis stream inside the kernel. Layer bounds (tile rows) must
+    be multiples of 8."""
+    _cuda(bits, t8, q, s, rs, z)
+    M, N = z.shape
+    ws = workspace(M, N, z.device)
+    check(lib.tcq_gemm_tcq_tc(_p(bits), _p(t8), _p(q), _p(s), _p(rs), _p(z), M, N, K, int(bounds[0]), int(bounds[1]), _p(ws),
+                              ws.numel() * 4, _stream()), 'tcq_gemm_tcq_tc')
+    _count('gemm_tcq_tc')
