@@ -52,6 +52,11 @@ const char* tcq_status_string(int status);
 int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4, float* scale,
             int M, int K, int ldq, void* stream);
 
+/* The per-token INT8 quantizer alone, without rotation (tcq_format.quantize_tokens, tcq_format.py:119-122), for
+ * W8A8 layers that are not rotated (the vision tower): x (M, K) BF16/F16/F32 -> q (M, K) int8,
+ * scale (M,) float32 = absmax / 127 (1 for an all-zero row). */
+int tcq_quantize(const void* x, int x_dtype, int8_t* q, float* scale, int M, int K, void* stream);
+
 /* Replaces kernels.pre2 (kernels.py:631-633; k_pre2, kernels.py:295-307): x = BF16(g * u) of two BF16 (M, K) inputs,
  * then as tcq_pre. */
 int tcq_pre2(const uint16_t* g, const uint16_t* u, const int8_t* su, int8_t* q, int32_t* q4, float* scale,

@@ -51,9 +51,11 @@ def test_int_mm_extremes(K):
 
 @pytest.mark.parametrize('M,Kd,N', cases.GEMMS)
 def test_int8_gemm_config3_golden(K, M, Kd, N):
-    """per-token quantizer (tcq_pre on an identity rotation is not the path here: the quantizer is
-    applied by the oracle) + tcgen05 GEMM + scale epilogue == the reference's BF16 output."""
+    """BASELINE config 3 end to end: per-token quantizer kernel + tcgen05 GEMM + scale epilogue == the reference."""
     a, w, sc = cases.gemm_inputs(M, Kd, N)
+    qd, sd = K.quantize(t(a, 'bf16'))
+    golden.check(f'gemm/{M}x{Kd}x{N}/q', n(qd))
+    golden.check(f'gemm/{M}x{Kd}x{N}/scale', n(sd))
     q, s = O.quantize_tokens(O.bf16_to_f32(a))
     out = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc))
     golden.check(f'gemm/{M}x{Kd}x{N}/out', n(out))

@@ -139,7 +139,7 @@ def test_rotate(K, T, D):
 
 
 @pytest.mark.parametrize('dt', ['bf16', 'f16', 'f32'])
-@pytest.mark.parametrize('Kd', [16, 48, 1152, 4304, 16384])
+@pytest.mark.parametrize('Kd', [16, 48, 1152, 4304, 12288, 16384])
 def test_pre_dtypes_and_widths(K, dt, Kd):
     M = 6
     x = cases.activations(f'pre{Kd}', M, Kd, dt)
@@ -196,7 +196,7 @@ def _mlp_inputs(M, N, seed):
 
 
 @pytest.mark.parametrize('act', ['gelu', 'silu'])
-@pytest.mark.parametrize('M,N', [(10, 4096), (3, 4304), (17, 1536), (2, 16384)])
+@pytest.mark.parametrize('M,N', [(10, 4096), (3, 4304), (17, 1536), (2, 16384), (5, 8192), (2, 12288)])
 def test_mlp_middles(K, act, M, N):
     acc, s, rs, sv, su, bias = _mlp_inputs(M, N, 0)
     lut = n(K.act_table(act))

@@ -18,6 +18,7 @@ SZ = ctypes.c_size_t
 SIGNATURES = {
     'tcq_abi_version': [],
     'tcq_status_string': [I],
+    'tcq_quantize': [P, I, P, P, I, I, P],
     'tcq_pre': [P, I, P, P, P, P, I, I, I, P],
     'tcq_pre2': [P, P, P, P, P, P, I, I, I, P],
     'tcq_pre_h': [P, I, P, P, P, I, I, I, P],

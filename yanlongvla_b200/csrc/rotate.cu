@@ -405,6 +405,41 @@ __global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, cons
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
+
+// Per-token INT8 quantizer without rotation (the W8A8 layers of config 3 / the vision tower): x (M, K) -> q (M, K),
+// scale (M,) = absmax / 127 (tcq_format.py:119-122). One block per token row; the row is read twice (max, quantize)
+// and stays in L1 / L2 between the two passes.
+template <int DT>
+__global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale, int M,
+                                               int K) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+    const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
+    float mx = 0.f;
+    for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
+        float v[16];
+        load16<DT>(xr + (size_t)16 * c * es, v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(v[k]));
+    }
+    mx = block_max(mx, red);
+    const float s = mx > 0.f ? mx / 127.f : 1.f;
+    if (threadIdx.x == 0) scale[tok] = s;
+    for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
+        float v[16];
+        load16<DT>(xr + (size_t)16 * c * es, v);
+        u32 w[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+            w[g] = (u32)(q8(v[4 * g], s) & 0xff) | ((u32)(q8(v[4 * g + 1], s) & 0xff) << 8) | ((u32)(q8(v[4 * g + 2], s) & 0xff) << 16) |
+                   ((u32)(q8(v[4 * g + 3], s) & 0xff) << 24);
+        *reinterpret_cast<uint4*>(q + (size_t)tok * K + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------------- host side
 int threads_for(int K) {
     int t = ((K >> 4) + 31) & ~31;
@@ -417,7 +452,9 @@ bool width_ok(int K) { return K > 0 && (K & 15) == 0 && K <= kMaxWidth; }
 
 template <class Kern, class... Args>
 int launch(Kern kern, dim3 grid, int threads, size_t smem, void* stream, Args... args) {
-    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    // Opt in above 46 KB of dynamic shared memory: the kernels also use up to 1 KB of static shared memory, and the
+    // default per-block limit (48 KB) covers both.
+    if (smem > 46 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -454,6 +491,21 @@ const char* tcq_status_string(int status) {
         case TCQ_ERR_DEVICE: return "no usable sm_100 device";
         case TCQ_ERR_WORKSPACE: return "workspace missing or too small";
         default: return "unknown status";
+    }
+}
+
+
+int tcq_quantize(const void* x, int x_dtype, int8_t* q, float* scale, int M, int K, void* stream) {
+    if (!x || !q || !scale) return TCQ_ERR_ARG;
+    if (M <= 0 || K <= 0 || (K & 15)) return TCQ_ERR_SHAPE;
+    if (!tcq_aligned(x, 16) || !tcq_aligned(q, 16)) return TCQ_ERR_ALIGN;
+    int T = ((K >> 4) + 31) & ~31;
+    if (T > 256) T = 256;
+    switch (x_dtype) {
+        case TCQ_DT_BF16: return launch(k_quant<TCQ_DT_BF16>, dim3(M), T, 0, stream, x, q, scale, M, K);
+        case TCQ_DT_F16: return launch(k_quant<TCQ_DT_F16>, dim3(M), T, 0, stream, x, q, scale, M, K);
+        case TCQ_DT_F32: return launch(k_quant<TCQ_DT_F32>, dim3(M), T, 0, stream, x, q, scale, M, K);
+        default: return TCQ_ERR_DTYPE;
     }
 }
 

@@ -468,7 +468,7 @@ int launch_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const flo
                    cudaStream_t st) {
     auto kern = k_gemm_w8<MT, RPW>;
     const int smem = K * M;
-    if (smem > 48 * 1024 && set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
+    if (smem > 46 * 1024 && set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
     const int rows_per_cta = (256 / 32) * RPW;
     const int grid = (N + rows_per_cta - 1) / rows_per_cta;
     cudaLaunchConfig_t cfg = {};

@@ -24,7 +24,7 @@ import torch
 
 from ._lib import DT_BF16, DT_F16, DT_F32, DT_I32, TcqError, check, lib
 
-__all__ = ['pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
+__all__ = ['quantize', 'pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
            'gemm_tcq', 'gemm_tcq_tc', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'device_error', 'gelu_table', 'silu_table', 'act_table',
            'TcqError', 'LAUNCHES']
 
@@ -94,6 +94,18 @@ def pre(x, su, q=None, q4=None, scale=None):
     dt = _dt(x, (torch.bfloat16, torch.float16, torch.float32), 'pre')
     check(lib.tcq_pre(_p(x), dt, _p(su), _p(q), _p(q4), _p(scale), M, K, 0 if q4 is None else q4.shape[1], _stream()), 'tcq_pre')
     _count('pre')
+
+
+def quantize(x, q=None, scale=None):
+    """Per-token INT8 quantizer without rotation (tcq_format.quantize_tokens): x (M, K) -> q (M, K) int8, scale (M,)."""
+    M, K = x.shape
+    q = torch.empty(M, K, dtype=torch.int8, device=x.device) if q is None else q
+    scale = torch.empty(M, dtype=torch.float32, device=x.device) if scale is None else scale
+    _cuda(x, q, scale)
+    check(lib.tcq_quantize(_p(x), _dt(x, (torch.bfloat16, torch.float16, torch.float32), 'quantize'), _p(q), _p(scale), M, K,
+                           _stream()), 'tcq_quantize')
+    _count('quantize')
+    return q, scale
 
 
 def pre2(g, u, su, q=None, q4=None, scale=None):

@@ -12,8 +12,10 @@ Runtimes (modules.py:3-8):
              (decode_chunk), the rest on the fly
 
 Token-count dispatch. The reference chooses the product by model part (action expert = few tokens). Here the group
-chooses per call: M <= SMALL_M tokens run the small-M products (fused trellis decode-GEMV or INT8-resident GEMV,
-FP32 scaled output), larger M run the tcgen05 INT8 GEMM (INT32 accumulators). Both give bit-identical results.
+chooses per call, from B200 measurements of the three products: M <= SIMT_MAX_M tokens run the SIMT products on q4
+words (fused trellis decode-GEMV, or the INT8-resident GEMV), FP32 scaled output; M <= TC_MAX_M tokens with the
+2-bit stream run the tensor-core fused decode-GEMM (FP32 scaled output); larger M, or INT8-resident weights, run the
+tcgen05 INT8 GEMM (INT32 accumulators) on resident or freshly decoded INT8 weights. All give bit-identical results.
 
 Layers that read the same tensor with identical input signs share one rotation + quantization and one product
 (q / k / v; gate / up): the group runs on the first member's call and the others return their slice (modules.py:10-12).
@@ -28,7 +30,8 @@ RUNTIMES = ('reference', 'resident', 'fly', 'hybrid')
 GROUPS = (('q_proj', 'k_proj', 'v_proj'), ('gate_proj', 'up_proj'))
 STATS = dict(group_runs=0, regroup_misses=0, fused_mlps=0)
 FUSE = dict(post3=True, mlp=True, split=True)
-SMALL_M = 16
+SIMT_MAX_M = 4
+TC_MAX_M = 32
 
 
 class Group:
@@ -50,6 +53,7 @@ class Group:
         self.t8 = torch.cat([L.t8.reshape(-1) for L in layers]).contiguous()
         self.bits = torch.cat([L.bits for L in layers]).contiguous() if mode != 'resident' else None
         self.bounds = [c // 16 for c in self.col0[1:]] + [1 << 30] * (3 - len(layers))
+        self.tc_ok = all(b % 8 == 0 for b in self.bounds[:len(layers) - 1])   # layer bounds on 128-row tiles
         self.W = None
         if mode in ('resident', 'chunk'):
             self.W = torch.empty(self.Ntot, self.K, dtype=torch.int8, device=dev)
@@ -75,7 +79,7 @@ class Group:
     def buffers(self, M, dev):
         """Quantized-activation buffer in the layout of this group's product, and the per-token scales."""
         s = torch.empty(M, dtype=torch.float32, device=dev)
-        if M <= SMALL_M:
+        if M <= SIMT_MAX_M:
             return dict(q4=torch.empty(self.K // 4, M, dtype=torch.int32, device=dev), scale=s)
         return dict(q=torch.empty(M, self.K, dtype=torch.int8, device=dev), scale=s)
 
@@ -85,8 +89,14 @@ class Group:
         return b
 
     def product(self, b):
-        """INT8 activations -> few tokens: FP32 z = ((float)acc * s) * rs (M, Ntot); many tokens: INT32 acc (M, Ntot)."""
+        """INT8 activations -> FP32 z = ((float)acc * s) * rs (M, Ntot) on the fused paths, INT32 acc (M, Ntot) on the
+        tcgen05 INT8 GEMM path."""
         if 'q' in b:
+            M = b['q'].shape[0]
+            if self.W is None and M <= TC_MAX_M and self.tc_ok:
+                z = torch.empty(M, self.Ntot, dtype=torch.float32, device=b['q'].device)
+                K.gemm_tcq_tc(self.bits, self.t8, b['q'], b['scale'], self.rs, z, self.K, self.bounds)
+                return z
             W = self.W if self.W is not None else self.decode(torch.empty(self.Ntot, self.K, dtype=torch.int8, device=b['q'].device))
             return K.int_mm(b['q'], W)
         M = b['q4'].shape[1]
@@ -266,7 +276,7 @@ def install(model, layers, runtime='fly', chunk_parts=('action_head',), mlp_acts
     names = list(layers)
     for name in names:
         m = model.get_submodule(name)
-        if not isinstance(m, (torch.nn.Linear, KLinear, RefLinear)):
+        if not hasattr(m, 'in_features') or not hasattr(m, 'out_features'):
             raise TypeError(f'{name} is {type(m).__name__}, not a Linear')
     info = dict(runtime=runtime, layers=len(names))
     if runtime == 'reference':
