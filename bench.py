@@ -17,6 +17,11 @@ exact INT8 product + scale epilogue) on a bounded sample of the layers, all host
 
 Multi-GPU (torchrun): every rank streams its own L layers (weak scaling, no collective on the data path); time = max
 over ranks of the device-timed region.
+
+The `policy` field measures the GR00T-style quantized policy (BASELINE configs 4 and 5, random-init weights, seeded
+synthetic observations): the action-chunk latency at batch 1 on one GPU, and actions/s of data-parallel replicas with
+--policy-batch observations per GPU (one CUDA-graph replay of the whole chunk per step, then one NCCL all-gather of
+the action chunks to rank 0), device-timed, max over ranks.
 """
 import argparse
 import json
@@ -231,6 +236,94 @@ def run_ours(args, rank, world, dist):
     return out
 
 
+# ------------------------------------------------------------------------------------------------ policy (configs 4, 5)
+def run_policy(args, rank, world, dist):
+    import torch
+    from yanlongvla_b200 import dp, modules, policy as P
+    dev = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    c = P.PolicyConfig()
+    model, _, info = P.build_policy(dev, args.policy_runtime, c, seed=0)
+    stream = torch.cuda.Stream(device=dev)
+
+    def capture(B, seed):
+        obs = P.synthetic_observations(B, c, dev, seed=seed)
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(2):
+                if args.policy_runtime == 'hybrid':
+                    modules.decode_chunk(model)
+                out = model(*obs)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                if args.policy_runtime == 'hybrid':
+                    modules.decode_chunk(model)
+                out = model(*obs)
+        torch.cuda.synchronize()
+        return g, obs, out
+
+    def time_steps(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        ts = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ts = torch.tensor(ts, device=dev)
+        if dist is not None:
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        ts = ts.cpu().tolist()
+        return float(np.median(ts)), float(np.percentile(ts, 95))
+
+    out = dict(runtime=args.policy_runtime, quantized_layers=dict(w2a8=info['layers'], w8a8=c.vit_layers * 6),
+               groups=info['groups'], fused_mlps=info['fused_mlps'])
+    # config 4: one observation, one GPU (every rank measures its own; max over ranks)
+    g1, _, _ = capture(1, 100 + rank)
+    out['chunk_ms_b1'], out['chunk_p95_ms_b1'] = time_steps(lambda: g1.replay(), args.policy_steps, 3)
+    del g1
+    # config 5: B = policy_batch * world observations, one shard per rank, one gather of the chunks to rank 0
+    B = args.policy_batch * world
+    b0, b1 = dp.shard(B, world, rank)
+    g, obs, acts = capture(b1 - b0, 200 + rank)
+
+    def dp_step():
+        g.replay()
+        with torch.cuda.stream(stream):
+            if dist is not None:
+                dp.gather_actions(acts, B)
+
+    med, p95 = time_steps(dp_step, args.policy_steps, 3)
+    out.update(batch=B, batch_per_gpu=b1 - b0, chunk_ms=med, chunk_p95_ms=p95, actions_per_s=B * c.chunk / (med * 1e-3),
+               gather='nccl all_gather_into_tensor of the (B/N, 16, 32) FP32 chunks' if dist is not None else 'none (1 GPU)',
+               finite=bool(torch.isfinite(acts).all().item()))
+    # e2e: observations from pinned host memory, actions back to the host, all inside the timed region
+    host = [t.cpu().pin_memory() for t in obs]
+    act_host = torch.empty(acts.shape, dtype=acts.dtype).pin_memory()
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for d, h in zip(obs, host):
+                d.copy_(h, non_blocking=True)
+        g.replay()
+        with torch.cuda.stream(stream):
+            if dist is not None:
+                dp.gather_actions(acts, B)
+            act_host.copy_(acts, non_blocking=True)
+
+    med_e, _ = time_steps(e2e_step, args.policy_steps, 3)
+    out['e2e'] = dict(chunk_ms=med_e, actions_per_s=B * c.chunk / (med_e * 1e-3),
+                      h2d_bytes_per_step=int(sum(h.numel() * h.element_size() for h in host)),
+                      d2h_bytes_per_step=int(act_host.numel() * act_host.element_size()))
+    del g
+    return {k: (round(v, 4) if isinstance(v, float) else v) for k, v in out.items()}
+
+
 # ------------------------------------------------------------------------------------------------ CPU reference arm
 def cpu_reference(sample_layers, threads):
     """The reference's CPU path of the metric (numpy restatement of tcq_format.py: windowed trellis read, hash decode,
@@ -294,6 +387,10 @@ def main():
     ap.add_argument('--layers', type=int, default=64)
     ap.add_argument('--ref-layers', type=int, default=2)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-policy', action='store_true')
+    ap.add_argument('--policy-runtime', default='fly', choices=['fly', 'resident', 'hybrid'])
+    ap.add_argument('--policy-batch', type=int, default=16, help='observations per GPU for the data-parallel policy')
+    ap.add_argument('--policy-steps', type=int, default=20)
     args = ap.parse_args()
     world = int(os.environ.get('WORLD_SIZE', 1))
     rank = int(os.environ.get('RANK', 0))
@@ -310,6 +407,8 @@ def main():
         torch.cuda.set_device(int(os.environ.get('LOCAL_RANK', 0)))
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
     out = run_ours(args, rank, world, dist)
+    if not args.no_policy:
+        out['policy'] = run_policy(args, rank, world, dist)
     if rank == 0:
         if not args.no_cpu_baseline:
             v, dt, nl = cpu_reference(args.ref_layers + 1, os.cpu_count())
