@@ -262,17 +262,19 @@ def run_policy(args, rank, world, dist):
         return g, obs, out
 
     def time_steps(fn, steps, warmup):
-        for _ in range(warmup):
-            fn()
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                fn()
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
         ts = []
         for _ in range(steps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            fn()
-            e1.record(stream)
+            with torch.cuda.stream(stream):             # the replay, the copies and the gather all run on `stream`
+                e0.record(stream)
+                fn()
+                e1.record(stream)
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ts = torch.tensor(ts, device=dev)
