@@ -406,8 +406,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(int(os.environ.get('LOCAL_RANK', 0)))
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+        local = int(os.environ.get('LOCAL_RANK', 0))
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=torch.device('cuda', local))
     out = run_ours(args, rank, world, dist)
     if not args.no_policy:
         out['policy'] = run_policy(args, rank, world, dist)

@@ -48,7 +48,10 @@ def init(backend='nccl', timeout_s=120):
     if dist.is_initialized():
         return dist.get_rank(), dist.get_world_size()
     rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    kw = {}
     if backend == 'nccl':
-        torch.cuda.set_device(int(os.environ.get('LOCAL_RANK', 0)))
-    dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+        local = int(os.environ.get('LOCAL_RANK', 0))
+        torch.cuda.set_device(local)
+        kw['device_id'] = torch.device('cuda', local)
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return rank, world
