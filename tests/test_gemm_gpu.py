@@ -30,7 +30,8 @@ def _rand(M, Kd, N, seed):
 
 
 @pytest.mark.parametrize('M,Kd,N', [(1, 128, 128), (3, 80, 48), (17, 1152, 320), (64, 2048, 2048), (100, 4304, 1152),
-                                    (256, 2048, 6144), (300, 1536, 1536), (513, 2048, 384), (1024, 8192, 2048)])
+                                    (160, 2048, 2048), (160, 8192, 2048), (512, 1152, 1152), (256, 2048, 6144),
+                                    (300, 1536, 1536), (513, 2048, 384), (1024, 8192, 2048)])
 def test_int_mm_exact(K, M, Kd, N):
     q, w = _rand(M, Kd, N, 0)
     acc = K.int_mm(t(q), t(w))
@@ -120,3 +121,15 @@ def test_gemm_tcq_tc_three_layers(K):
     K.gemm_tcq_tc(bits, t8, t(q), t(s), rs, z, 2048, bounds=(128, 160))
     zr = np.concatenate([O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs) for L in Ls], 1)
     assert np.array_equal(n(z), zr)
+
+
+@pytest.mark.parametrize('M,Kd,N', [(512, 1152, 1152), (512, 1152, 4304), (512, 4304, 1152), (2048, 1152, 1152)])
+def test_int8_gemm_vision_shapes(K, M, Kd, N):
+    """The vision tower's W8A8 products (BF16 scaled epilogue) at the policy's token counts."""
+    r = cases.rng('vit', M, Kd, N)
+    a = (r.standard_normal((M, Kd)) * 2).astype(np.float32)
+    w = r.integers(-127, 128, size=(N, Kd), dtype=np.int32).astype(np.int8)
+    sc = r.uniform(1e-4, 1e-3, N).astype(np.float32)
+    q, s = O.quantize_tokens(a)
+    out = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc))
+    assert np.array_equal(n(out), O.int8_gemm_scaled(q, w, s[:, 0], sc))

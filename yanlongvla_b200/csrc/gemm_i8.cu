@@ -122,10 +122,10 @@ __device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&v)[32]) {
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_BF16 = 2 };
 
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int MODE, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
-          const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K) {
+          const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K, int ks) {
     constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
     constexpr u32 TMEM_COLS = 2 * BN;          // two accumulator buffers; BN in {32, 64, 128, 256} -> power of two
     constexpr u32 IDESC = idesc_i8(BN);
@@ -139,7 +139,9 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
     const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
               tempty0 = smem_u32(bars + 2 * STAGES + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + BN - 1) / BN, tiles = tiles_n * tiles_m;
+    // Work item = (channel tile, token tile, K split); with ks > 1 (INT32 output only) the splits add their partial
+    // sums into the zero-filled output with integer atomics (exact).
+    const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + BN - 1) / BN, tiles = tiles_n * tiles_m * ks;
     const int KB = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -177,8 +179,9 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
             for (int s = 0; s < STAGES; ++s) armed[s] = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int tn = tile % tiles_n, tm = tile / tiles_n;
-                for (int kb = 0; kb < KB; ++kb) {
+                const int sp = tile % ks, tt = tile / ks, tn = tt % tiles_n, tm = tt / tiles_n;
+                const int kb0 = KB * sp / ks, kb1 = KB * (sp + 1) / ks;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag)) { ok = false; break; }
                     mbar_expect_tx(full0 + 8 * stage, A_BYTES + B_BYTES);
                     tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmW, full0 + 8 * stage, kb * BK, tn * BM);
@@ -200,18 +203,20 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
             bool ok = true;
             int committed = -1;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
+                const int sp = tile % ks;
+                const int kb0 = KB * sp / ks, kb1 = KB * (sp + 1) / ks;
                 const int a = it & 1;
                 const u32 aph = (it >> 1) & 1;
                 if (!mbar_wait(tempty0 + 8 * a, aph ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const u32 d = tmem + a * BN;
-                for (int kb = 0; kb < KB; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full0 + 8 * stage, phase, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const u32 aaddr = smem_u32(sA + stage * A_BYTES), baddr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 32; ++k)
-                        mma_i8(d, sw128_desc(aaddr + 32 * k), sw128_desc(baddr + 32 * k), IDESC, (kb | k) != 0);
+                        mma_i8(d, sw128_desc(aaddr + 32 * k), sw128_desc(baddr + 32 * k), IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
                     mma_commit(empty0 + 8 * stage);
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -233,7 +238,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
             const u32 aph = (it >> 1) & 1;
             if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
             tc_fence_after();
-            const int tn = tile % tiles_n, tm = tile / tiles_n;
+            const int tt = tile / ks, tn = tt % tiles_n, tm = tt / tiles_n;
             const int ch = tn * BM + 32 * q + lane, m0 = tm * BN;
             const bool chok = ch < N;
             const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
@@ -249,7 +254,8 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
                         if (tok < M) {
                             const size_t o = (size_t)tok * N + ch;
                             if (MODE == OUT_I32) {
-                                reinterpret_cast<int*>(out)[o] = (int)v[j];
+                                if (!SPLIT) reinterpret_cast<int*>(out)[o] = (int)v[j];
+                                else atomicAdd(reinterpret_cast<int*>(out) + o, (int)v[j]);
                             } else {
                                 const float z = ((float)(int)v[j] * s_tok[tok]) * sc;
                                 if (MODE == OUT_F32) reinterpret_cast<float*>(out)[o] = z;
@@ -508,15 +514,16 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows)
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int MODE>
-int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
+template <int BN, int STAGES, int MODE, bool SPLIT = false>
+int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K, int ks,
               cudaStream_t st) {
     CUtensorMap tmW, tmQ;
     if (!make_map(&tmW, W, N, K, BM) || !make_map(&tmQ, q, M, K, BN)) return TCQ_ERR_ARG;
-    auto kern = k_gemm_i8<BN, STAGES, MODE>;
+    auto kern = k_gemm_i8<BN, STAGES, MODE, SPLIT>;
     const int smem = 1024 + STAGES * (BM + BN) * BK + (2 * STAGES + 4) * 8 + 16;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
-    const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
+    if (ks > 1 && cudaMemsetAsync(out, 0, (size_t)M * N * sizeof(int), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
+    const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN) * ks;
     const int grid = tiles < sms() ? tiles : sms();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -528,18 +535,27 @@ int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K, ks) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
 }
 
+// Token-tile width: 256 while that still gives a quarter of the SMs a tile (wide tiles re-read the weights least);
+// otherwise the widest of 128 / 64 / 32 that fills half the SMs, so small-M products do not run on a handful of SMs.
+// An INT32 product with too few tiles even at 32 is split along K as well (integer atomics into the zeroed output).
 template <int MODE>
 int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
              cudaStream_t st) {
-    if (M <= 32) return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
-    if (M <= 64) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
-    if (M <= 128) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
-    return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
+    const int ct = (N + BM - 1) / BM, half = sms() / 2, KB = (K + BK - 1) / BK;
+    auto tiles = [&](int bn) { return ct * ((M + bn - 1) / bn); };
+    if (M > 128 && tiles(256) >= sms() / 4) return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
+    if (M > 64 && tiles(128) >= half) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
+    if (M > 32 && tiles(64) >= half) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
+    if (MODE == OUT_I32 && tiles(32) < half) {
+        int ks = sms() / tiles(32);
+        if (ks > KB / 2) ks = KB / 2;
+        if (ks > 1) return launch_i8<32, 8, MODE, true>(q, W, out, s_tok, s_ch, M, N, K, ks, st);
+    }
+    return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
 }
-
 
 template <int BN, int STAGES>
 int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z, int M, int N,
