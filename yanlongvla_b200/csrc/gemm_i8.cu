@@ -13,70 +13,22 @@
 //             epilogue of tile i overlaps the MMAs of tile i + 1.
 // Every mbarrier wait is bounded (about 2 s): on expiry the kernel sets a device error flag, stops, waits (bounded)
 // for its copies and MMAs in flight, frees TMEM and returns; tcq_device_error() reports the flag.
-#include <cuda.h>
-
+#include "tma.cuh"
 #include "trellis_common.cuh"
 
 __device__ int g_tcq_device_error;
 
 namespace {
 
+using namespace tcq;
+
 constexpr int BM = 128;           // channels per tile
 constexpr int BK = 128;           // K bytes per stage
 constexpr int kThreads = 192;
-constexpr unsigned long long kWaitNs = 2000000000ull;
 
-__device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(u32 bar, u32 bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(u32 bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(u32 bar, u32 parity) {
-    u32 ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ unsigned long long gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Bounded wait for the phase of parity `parity` to complete. Returns false when the CTA was aborted or the wait
-// expired (then the device error flag is set and the CTA abort flag raised).
+// Bounded wait that reports through this file's device error flag.
 __device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, volatile int* abort_flag, unsigned long long limit = kWaitNs) {
-    if (mbar_try(bar, parity)) return true;
-    const unsigned long long t0 = gtime();
-    for (u32 i = 1;; ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if ((i & 127) == 0) {
-            if (*abort_flag) return false;
-            if (gtime() - t0 > limit) {
-                atomicOr(&g_tcq_device_error, 1);
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(u32 dst, const CUtensorMap* map, u32 bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(map), "r"(bar), "r"(x), "r"(y)
-        : "memory");
+    return mbar_wait_bounded(bar, parity, abort_flag, &g_tcq_device_error, limit);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -481,24 +433,6 @@ int sms() {
         if (cudaDeviceGetAttribute(&g_sms_i8, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_sms_i8 <= 0) g_sms_i8 = 148;
     }
     return g_sms_i8;
-}
-
-// cuTensorMapEncodeTiled is a driver entry point; it is resolved through the runtime at first use so that the library
-// does not link libcuda (it loads on machines without a driver, where only the host-side validation is exercised).
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
-                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
 }
 
 // 2-D int8 tensor map over a row-major (rows, K) matrix: box = 128 bytes of K x box_rows rows, 128-byte swizzle,

@@ -64,6 +64,27 @@ TCQ_HD int block_of(int i, int K) { return 1 << (31 - __clz(i ^ K)); }
 // banks; 32 consecutive indices still map to 32 distinct banks.
 TCQ_HD int swz(int i) { return i ^ (((i >> 5) & 3) << 2); }
 
+// ---------------------------------------------------------------------------------------------------- division
+// Exact n / d for 0 <= n < 2^31 by a multiply-high and a shift (Granlund and Montgomery, "Division by invariant
+// integers using multiplication", 1994): with l = ceil(log2 d) and m = ceil(2^(31+l) / d) < 2^32, the error of
+// n * m / 2^(31+l) against n / d stays below 1/d as long as n * d < 2^(31+l), which n < 2^31 guarantees.
+struct FastDiv {
+    unsigned d, m, sh;    // d == 1: the identity
+};
+
+static inline FastDiv make_fastdiv(unsigned d) {
+    FastDiv f{d, 0u, 0u};
+    if (d > 1) {
+        int l = 0;
+        while ((1ull << l) < d) ++l;
+        f.m = (unsigned)(((1ull << (31 + l)) + d - 1) / d);
+        f.sh = (unsigned)(l - 1);
+    }
+    return f;
+}
+
+TCQ_HD unsigned fdiv(unsigned n, const FastDiv& f) { return f.d == 1 ? n : __umulhi(n, f.m) >> f.sh; }
+
 // ---------------------------------------------------------------------------------------------------- loads
 TCQ_HD uint4 ldg_nc_v4(const void* p) {
     uint4 r;
@@ -77,6 +98,11 @@ TCQ_HD uint4 ldg_stream_v4(const void* p) {
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
     return r;
+}
+
+// Bulk prefetch of [p, p + bytes) into L2 (no register or shared-memory destination); p and bytes multiples of 16.
+TCQ_HD void prefetch_l2_bulk(const void* p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // ---------------------------------------------------------------------------------------------------- PDL

@@ -17,6 +17,8 @@
 //   * decoded pairs are packed with one byte_perm per two pairs and consumed by dp4a in registers.
 #include <mutex>
 
+#include <algorithm>
+
 #include "trellis_common.cuh"
 
 namespace {
@@ -97,9 +99,14 @@ struct Parts {
     int cta0[4];    // first CTA of layer l; cta0[n] = grid
     int tr0[4];     // first tile row of layer l; tr0[n] = N / 16
     int slot[3];    // table slot (0..2) of layer l in t8
+    int uq[3];      // units of layer l per CTA: CTA c of the layer takes uq + (c < ur) units, c * uq + min(c, ur) first
+    int ur[3];
+    FastDiv fS;     // division by S, the units per tile row
+    int pf_lead;    // > 0 (one layer only): CTA c prefetches into L2 the stream of CTA c + pf_lead
 };
 
-constexpr int kMaxRows = 24;    // tile rows one CTA may touch (the launcher bounds the units per CTA accordingly)
+constexpr int kMaxRows = 24;
+    // tile rows one CTA may touch (the launcher bounds the units per CTA accordingly)
 
 // Sum V = RPT x MT accumulators over the lanes that hold the same row group (lanes differing in bits >= log2(LT)) by
 // recursive halving: each exchange step sends half of the remaining values and keeps the other half (16 values over
@@ -162,43 +169,74 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     extern __shared__ __align__(128) u32 tab[];
     __shared__ __align__(16) u16 pairs[512];
     __shared__ int racc[kMaxRows * RV];
+    __shared__ float srs[kMaxRows * 16];           // row scales of this CTA's tile rows
+    __shared__ float ss[MT];                       // token scales
     pdl_launch_dependents();
     // This CTA's layer (selected without dynamic indexing of the parameter arrays).
-    int cb = parts.cta0[0], ce = parts.cta0[1], tb = parts.tr0[0], te = parts.tr0[1], slot = parts.slot[0];
+    int cb = parts.cta0[0], tb = parts.tr0[0], slot = parts.slot[0], uq = parts.uq[0], ur = parts.ur[0];
     if (parts.n > 1 && (int)blockIdx.x >= parts.cta0[1]) {
-        cb = parts.cta0[1]; ce = parts.cta0[2]; tb = parts.tr0[1]; te = parts.tr0[2]; slot = parts.slot[1];
+        cb = parts.cta0[1]; tb = parts.tr0[1]; slot = parts.slot[1]; uq = parts.uq[1]; ur = parts.ur[1];
     }
     if (parts.n > 2 && (int)blockIdx.x >= parts.cta0[2]) {
-        cb = parts.cta0[2]; ce = parts.cta0[3]; tb = parts.tr0[2]; te = parts.tr0[3]; slot = parts.slot[2];
+        cb = parts.cta0[2]; tb = parts.tr0[2]; slot = parts.slot[2]; uq = parts.uq[2]; ur = parts.ur[2];
     }
-    const int tiles = K >> 4, S = (tiles + TPU - 1) / TPU;
-    const int U = (te - tb) * S;                   // < 2^31: checked by the launcher
-    const int G = ce - cb, c = blockIdx.x - cb;
-    const int ub = (int)((long long)U * c / G), ue = (int)((long long)U * (c + 1) / G);
+    // Units (tile row, TPU-tile segment) u = row * S + segment; this CTA takes [ub, ue). No divisions: the split
+    // comes from the launcher's quotient / remainder, rows from a multiply-high.
+    const int tiles = K >> 4, S = (int)parts.fS.d;
+    const int c = blockIdx.x - cb;
+    const int ub = c * uq + (c < ur ? c : ur), ue = ub + uq + (c < ur ? 1 : 0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int tin = lane / LT, rg = lane % LT;
     const u32 lane4 = 4u * lane;
-    const int row_first = ub / S;
-    const int nrows = ub < ue ? (ue - 1) / S - row_first + 1 : 0;
+    const int row_first = (int)fdiv(ub, parts.fS);
+    const int nrows = ub < ue ? (int)fdiv(ue - 1, parts.fS) - row_first + 1 : 0;
 
+    // The 1 KB table is the CTA's first memory request: the table build waits for it, and under a full HBM stream
+    // a request queued behind this CTA's weight loads returns about a microsecond later.
+    uint4 t8v = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < 64) t8v = __ldg(reinterpret_cast<const uint4*>(t8 + 1024 * slot) + threadIdx.x);
+    // The CTAs of a launch start one by one, in index order, as the previous launch's CTAs leave their SMs (over
+    // about one launch time). When each CTA has little work, CTA c asks L2 for the stream of CTA c + pf_lead, which
+    // starts about a DRAM latency later and then finds its weights in L2 instead of waiting on DRAM.
+    if (parts.pf_lead && threadIdx.x == 0) {
+        const int c2 = c + parts.pf_lead;
+        if (c2 < parts.cta0[1] - parts.cta0[0]) {
+            const int b2 = c2 * uq + (c2 < ur ? c2 : ur), e2 = b2 + uq + (c2 < ur ? 1 : 0);
+            const int r0 = (int)fdiv(b2, parts.fS), r1 = (int)fdiv(e2 - 1, parts.fS);
+            const long long t0 = (long long)(tb + r0) * tiles + (b2 - r0 * S) * TPU;
+            const long long t1 = (long long)(tb + r1) * tiles + std::min(tiles, (e2 - 1 - r1 * S) * TPU + TPU);
+            const char* p0 = reinterpret_cast<const char*>(bits) + t0 * 64;
+            for (long long o = 0; o < (t1 - t0) * 64; o += 65536)
+                prefetch_l2_bulk(p0 + o, (unsigned)std::min((t1 - t0) * 64 - o, 65536ll));
+        }
+    }
     int u = ub + warp;
+    int rrel = (int)fdiv(u, parts.fS), seg = u - rrel * S;    // this warp's unit, relative tile row and segment
     u32 Wn[RPT + 1];
     if (u < ue) {
-        const int tc = (u % S) * TPU + tin;
-        if (tc < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + u / S) * tiles + tc, rg, Wn);   // weights: before the wait
+        const int tc = seg * TPU + tin;
+        if (tc < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rrel) * tiles + tc, rg, Wn);   // weights: before the wait
     }
     for (int i = threadIdx.x; i < nrows * RV; i += blockDim.x) racc[i] = 0;
-    build_table_i8(tab, pairs, t8 + 1024 * slot);
+    // Epilogue operands are fetched now and held in registers until the decode is done, so that their latency hides
+    // behind it: the row scales (layer constants) before the dependency wait, the token scales right after it.
+    const int nrs = nrows * 16;                    // <= kMaxRows * 16 <= kThreads
+    const float rsv = (int)threadIdx.x < nrs ? __ldg(rs + (size_t)(tb + row_first) * 16 + threadIdx.x) : 0.f;
+    if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = t8v;
+    __syncthreads();
+    fill_table_i8_nt<kThreads>(tab, pairs);
     __syncthreads();
     pdl_wait();                                    // activations / scales come from the previous kernel
+    const float sv = (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
     for (; u < ue; u += nw) {
-        const int rrel = u / S, tc = (u - rrel * S) * TPU + tin;
+        const int tc = seg * TPU + tin;
         u32 W[RPT + 1];
+        int rn = rrel, sn = seg + nw;              // the warp's next unit
+        while (sn >= S) { sn -= S; ++rn; }
 #pragma unroll
         for (int a = 0; a <= RPT; ++a) W[a] = Wn[a];
-        const int un = u + nw;
-        if (un < ue) {
-            const int rn = un / S, tcn = (un - rn * S) * TPU + tin;
+        if (u + nw < ue) {
+            const int tcn = sn * TPU + tin;
             if (tcn < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rn) * tiles + tcn, rg, Wn);
         }
         int acc[V];
@@ -235,16 +273,21 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
                 if (idx % MT < M) atomicAdd(ra + idx, acc[i]);
             }
         }
+        rrel = rn;
+        seg = sn;
     }
+    if ((int)threadIdx.x < nrs) srs[threadIdx.x] = rsv;
+    if (threadIdx.x < MT) ss[threadIdx.x] = sv;
     __syncthreads();
     for (int r = warp; r < nrows; r += nw) {
         const int rrel = row_first + r, trow = tb + rrel;
         const int a0 = rrel * S, a1 = a0 + S;
         const int* src = racc + r * RV;
+        const float* rsr = srs + r * 16;
         if (a0 >= ub && a1 <= ue) {                // the whole tile row was summed here
             for (int i = lane; i < RV; i += 32) {
                 const int rr = i / MT, m = i % MT, row = trow * 16 + rr;
-                if (m < M) z[(size_t)m * N + row] = ((float)src[i] * s[m]) * rs[row];
+                if (m < M) z[(size_t)m * N + row] = ((float)src[i] * ss[m]) * rsr[rr];
             }
             continue;
         }
@@ -265,7 +308,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
                 if (m < M) {
                     const size_t o = (size_t)m * N + row;
                     const int v = atomicExch(ws_acc + o, 0);      // read and clear; lanes issue these in parallel
-                    z[o] = ((float)v * s[m]) * rs[row];
+                    z[o] = ((float)v * ss[m]) * rsr[rr];
                 }
             }
             if (lane == 0) ws_cnt[trow] = 0;
@@ -396,8 +439,6 @@ int decode_grid(int m, int n) {
 template <int MT, int LT>
 int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
                     int M, int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
-    auto kern = k_gemm_tcq<MT, LT>;
-    if (set_smem(kern, kTabBytes)) return TCQ_ERR_LAUNCH;
     const int TPU = 32 / LT, tiles = K >> 4, S = (tiles + TPU - 1) / TPU, R = N >> 4;
     Parts p{};
     int bounds[4] = {0, nb0 < R ? nb0 : R, nb1 < R ? nb1 : R, R};
@@ -424,16 +465,25 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
         p.cta0[nl] = cta;
         p.tr0[nl] = bounds[l];
         p.slot[nl] = l;
+        p.uq[nl] = (int)(Ul / g);
+        p.ur[nl] = (int)(Ul % g);
         cta += (int)g;
         ++nl;
     }
     p.n = nl;
     p.cta0[nl] = cta;
     p.tr0[nl] = R;
+    p.fS = make_fastdiv((unsigned)S);
+    int max_units = 0;
+    for (int l = 0; l < nl; ++l) max_units = std::max(max_units, p.uq[l] + (p.ur[l] > 0 ? 1 : 0));
+    p.pf_lead = nl == 1 && max_units <= 2 * (kThreads / 32) ? std::max(1, (cta * 5) / 16) : 0;
+    auto kern = k_gemm_tcq<MT, LT>;
+    const int smem = kTabBytes;
+    if (set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cta);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kTabBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -449,13 +499,14 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
     return TCQ_OK;
 }
 
-// Lanes per tile: for M = 1 on layers with fewer tiles than threads on the machine, four lanes split a tile's rows
-// (a warp covers 8 tiles, every SM gets many small units and the load latency hides); on larger layers one lane per
-// tile (fewest instructions per weight). M <= 4: 4 lanes; larger M: one lane per token slot (MT lanes).
+// Lanes per tile: for M = 1, one lane per tile (fewest instructions per weight) once the layer has at least 3/4 as
+// many tiles as the machine has threads (4096 x 4096 and up); on smaller layers two or four lanes split a tile's
+// rows so that every warp still gets work. M <= 4: 4 lanes; larger M: one lane per token slot (MT lanes).
 int dispatch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z, int M,
                       int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
-    const long long tiles = (long long)(N >> 4) * (K >> 4);
-    if (M == 1 && tiles >= (long long)num_sms() * kThreads) return launch_gemm_tcq<1, 1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    const long long tiles = (long long)(N >> 4) * (K >> 4), lanes = (long long)num_sms() * kThreads;
+    if (M == 1 && tiles * 4 >= lanes * 3) return launch_gemm_tcq<1, 1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M == 1 && tiles * 8 >= lanes * 3) return launch_gemm_tcq<1, 2>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
     if (M == 1) return launch_gemm_tcq<1, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
     if (M == 2) return launch_gemm_tcq<2, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
     if (M <= 4) return launch_gemm_tcq<4, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);

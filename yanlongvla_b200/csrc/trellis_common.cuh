@@ -19,8 +19,7 @@ __device__ __forceinline__ void stage_pairs(u16* pairs, const void* __restrict__
     __syncthreads();
 }
 
-__device__ __forceinline__ void build_table_i8(u32* tab, u16* pairs, const i8* __restrict__ t8) {
-    stage_pairs(pairs, t8);
+__device__ __forceinline__ void fill_table_i8(u32* tab, const u16* pairs) {
     // Thread t writes 16-byte slot (t & 7) of keys k and k + 512 (the same pair, first coordinate negated) for
     // k = t >> 3, + blockDim / 8, ...: one shared load per two stores.
     uint4* t4 = reinterpret_cast<uint4*>(tab);
@@ -31,6 +30,30 @@ __device__ __forceinline__ void build_table_i8(u32* tab, u16* pairs, const i8* _
         t4[k * 8 + slot] = make_uint4(ep, ep, ep, ep);
         t4[(k + 512) * 8 + slot] = make_uint4(en, en, en, en);
     }
+}
+
+// The same fill for a block of exactly NT threads: all shared loads first, then the stores (no load -> store chain
+// per iteration).
+template <int NT>
+__device__ __forceinline__ void fill_table_i8_nt(u32* tab, const u16* pairs) {
+    constexpr int IT = 512 / (NT / 8);
+    uint4* t4 = reinterpret_cast<uint4*>(tab);
+    const int slot = threadIdx.x & 7, k0 = threadIdx.x >> 3;
+    u32 pr[IT];
+#pragma unroll
+    for (int j = 0; j < IT; ++j) pr[j] = pairs[k0 + j * (NT / 8)];
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+        const int k = k0 + j * (NT / 8);
+        const u32 ep = pr[j] & 0xffffu, en = ((0u - pr[j]) & 0xffu) | (pr[j] & 0xff00u);
+        t4[k * 8 + slot] = make_uint4(ep, ep, ep, ep);
+        t4[(k + 512) * 8 + slot] = make_uint4(en, en, en, en);
+    }
+}
+
+__device__ __forceinline__ void build_table_i8(u32* tab, u16* pairs, const i8* __restrict__ t8) {
+    stage_pairs(pairs, t8);
+    fill_table_i8(tab, pairs);
 }
 
 // BF16 entry: low half = BF16(v0) with the sign bit flipped for sign keys, high half = BF16(v1) (kernels.py:320-337).
