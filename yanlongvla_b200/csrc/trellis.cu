@@ -106,6 +106,7 @@ struct Parts {
 };
 
 constexpr int kMaxRows = 24;
+constexpr int kUnitBytes = 32 * 64;    // one warp's unit of one-lane-per-tile work: 32 tiles
     // tile rows one CTA may touch (the launcher bounds the units per CTA accordingly)
 
 // Sum V = RPT x MT accumulators over the lanes that hold the same row group (lanes differing in bits >= log2(LT)) by
@@ -212,10 +213,24 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     }
     int u = ub + warp;
     int rrel = (int)fdiv(u, parts.fS), seg = u - rrel * S;    // this warp's unit, relative tile row and segment
+    // CO (one lane per tile): a warp loads its unit's 2 KB with row-contiguous 16-byte loads (4 cache lines per
+    // instruction instead of 16, which would hold up the table request in the load/store pipeline) and turns it
+    // into one tile per lane through a 2 KB staging area in shared memory. The staging layout keeps 16-byte chunk c
+    // of tile t at chunk c ^ ((t >> 1) & 3): both the row-contiguous stores and the per-tile reads are conflict-free.
+    constexpr bool CO = LT == 1;
+    char* stage = reinterpret_cast<char*>(tab + kTabBytes / 4) + warp * kUnitBytes;
+    auto load_unit = [&](int r, int sg, uint4 (&L)[4]) {
+        const uint4* base = reinterpret_cast<const uint4*>(bits + ((size_t)(tb + r) * tiles + (size_t)sg * TPU) * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            L[j] = sg * TPU + 8 * j + (lane >> 2) < tiles ? ldg_stream_v4(base + 32 * j + lane) : make_uint4(0, 0, 0, 0);
+    };
     u32 Wn[RPT + 1];
+    uint4 Ln[4];
     if (u < ue) {
         const int tc = seg * TPU + tin;
-        if (tc < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rrel) * tiles + tc, rg, Wn);   // weights: before the wait
+        if (CO) load_unit(rrel, seg, Ln);                                      // weights: before the wait
+        else if (tc < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rrel) * tiles + tc, rg, Wn);
     }
     for (int i = threadIdx.x; i < nrows * RV; i += blockDim.x) racc[i] = 0;
     // Epilogue operands are fetched now and held in registers until the decode is done, so that their latency hides
@@ -233,11 +248,29 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         u32 W[RPT + 1];
         int rn = rrel, sn = seg + nw;              // the warp's next unit
         while (sn >= S) { sn -= S; ++rn; }
+        if constexpr (CO) {
 #pragma unroll
-        for (int a = 0; a <= RPT; ++a) W[a] = Wn[a];
-        if (u + nw < ue) {
-            const int tcn = sn * TPU + tin;
-            if (tcn < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rn) * tiles + tcn, rg, Wn);
+            for (int j = 0; j < 4; ++j) {
+                const int t = 8 * j + (lane >> 2), c = lane & 3;
+                *reinterpret_cast<uint4*>(stage + 64 * t + 16 * (c ^ ((t >> 1) & 3))) = Ln[j];
+            }
+            __syncwarp();
+            const char* mine = stage + 64 * lane;
+            const int x = (lane >> 1) & 3;
+            const uint4 c0 = *reinterpret_cast<const uint4*>(mine + 16 * (0 ^ x)), c1 = *reinterpret_cast<const uint4*>(mine + 16 * (1 ^ x)),
+                        c2 = *reinterpret_cast<const uint4*>(mine + 16 * (2 ^ x)), c3 = *reinterpret_cast<const uint4*>(mine + 16 * (3 ^ x));
+            __syncwarp();
+            const u32 all[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+#pragma unroll
+            for (int a = 0; a <= RPT; ++a) W[a] = all[a & 15];
+            if (u + nw < ue) load_unit(rn, sn, Ln);
+        } else {
+#pragma unroll
+            for (int a = 0; a <= RPT; ++a) W[a] = Wn[a];
+            if (u + nw < ue) {
+                const int tcn = sn * TPU + tin;
+                if (tcn < tiles) load_tile_rows<RPT>(bits, (size_t)(tb + rn) * tiles + tcn, rg, Wn);
+            }
         }
         int acc[V];
 #pragma unroll
@@ -478,7 +511,7 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
     for (int l = 0; l < nl; ++l) max_units = std::max(max_units, p.uq[l] + (p.ur[l] > 0 ? 1 : 0));
     p.pf_lead = nl == 1 && max_units <= 2 * (kThreads / 32) ? std::max(1, (cta * 5) / 16) : 0;
     auto kern = k_gemm_tcq<MT, LT>;
-    const int smem = kTabBytes;
+    const int smem = kTabBytes + (LT == 1 ? (kThreads / 32) * kUnitBytes : 0);
     if (set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cta);
