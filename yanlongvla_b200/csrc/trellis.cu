@@ -275,17 +275,20 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         int acc[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] = 0;
-        if (tc < tiles) {
+        // CO: tiles past the end of the tile row hold zero words and get zero activations, so the decode runs on
+        // every lane without a branch (their products add nothing).
+        if (CO || tc < tiles) {
             int act[4][MT];
             const int* qa = q4 + (size_t)4 * tc * M;
             if (MT == 1 && act_vec) {
-                const int4 v = __ldg(reinterpret_cast<const int4*>(qa));
+                int4 v = make_int4(0, 0, 0, 0);
+                if (!CO || tc < tiles) v = __ldg(reinterpret_cast<const int4*>(qa));
                 act[0][0] = v.x; act[1][0] = v.y; act[2][0] = v.z; act[3][0] = v.w;
             } else {
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
 #pragma unroll
-                    for (int m = 0; m < MT; ++m) act[e][m] = (m < M) ? __ldg(qa + e * M + m) : 0;
+                    for (int m = 0; m < MT; ++m) act[e][m] = (m < M && tc < tiles) ? __ldg(qa + e * M + m) : 0;
             }
 #pragma unroll
             for (int a = 0; a < RPT; ++a) {
