@@ -39,6 +39,11 @@ M_N = 4096                      # config 1: W is 4096 x 4096
 TOKENS = 1
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_gemm_tcq<1, 1> launch on a 4096 x 4096 layer, M = 1, from
+# the ncu capture summarized in profiles/gemm_tcq_m1_4096x4096.md (cold cache; the algorithmic bytes are 4,232,196).
+NCU_TRAFFIC_BYTES = 4244992
+
+
 def layer_bytes(m, n, M):
     """Algorithmic HBM bytes of one decode-GEMV launch: 2-bit stream m*n/4 + INT8 table 1024 + row scales 4m +
     INT8 activations M*n + token scales 4M + FP32 outputs 4*M*m."""
@@ -225,8 +230,10 @@ def run_ours(args, rank, world, dist):
                     launch='one CUDA graph per step, one launch per layer, programmatic dependent launch',
                     parallelism='dp%d (independent layers per GPU, no collective)' % world),
         roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
-                      traffic=None, peak_kind=peak_kind,
-                      note='achieved = bytes_per_layer / (graph step time / layers); includes inter-launch gaps'),
+                      traffic=NCU_TRAFFIC_BYTES, peak_kind=peak_kind,
+                      note='achieved = bytes_per_layer / (graph step time / layers); includes inter-launch gaps. '
+                           'traffic: DRAM bytes read + written by one launch of this kernel at this shape '
+                           '(ncu --set full capture, profiles/gemm_tcq_m1_4096x4096.md)'),
         e2e=dict(value=round(e2e_gbs, 1), unit='GB/s', h2d_bytes_per_step=int(xh.numel() * 2), d2h_bytes_per_step=int(yh.numel() * 2),
                  ms_per_step=round(e2e_ms, 4), path='kernels.pre -> gemm_tcq -> post per layer (whole quantized Linear)'),
         gpu_launches=args.steps * L,
