@@ -52,3 +52,62 @@ def kernel_classes(graph, warm=3):
     return dict(wall_ms=wall, kernel_ms=total, gaps_ms=max(wall - total, 0.0), launches=sum(launches.values()),
                 by_class_ms={k: round(v, 3) for k, v in sorted(by.items(), key=lambda kv: -kv[1])},
                 launches_by_class=dict(launches), top=[(nm, round(d, 3)) for nm, d in top.most_common(12)])
+
+
+# ----------------------------------------------------------------------------------------------- profiling cases
+# Small, seeded invocations of one kernel each, for a profiler to capture (nothing is timed or checked here):
+#   python -m yanlongvla_b200.profile gemv [--n 4096] [--k 4096] [--tokens 1] [--launches 4]
+#   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--launches 4]
+# `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
+# kernels.int_mm on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
+# are warm in the driver and the code caches.
+def _case_gemv(n, k, tokens, launches):
+    from . import kernels as K
+    from .tcq_format import snap
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(11)
+    bits = torch.randint(-32768, 32768, ((n // 16) * (k // 16), 32), dtype=torch.int32, device=dev, generator=g).to(torch.int16)
+    t8, rs, _ = snap((torch.randn(512, 2, device=dev, generator=g) * 0.968).half(),
+                     (torch.rand(n, device=dev, generator=g) * 0.02 + 0.005).half())
+    q4 = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // 4, tokens), dtype=torch.int32, device=dev, generator=g)
+    s = torch.rand(tokens, device=dev, generator=g)
+    z = torch.empty(tokens, n, device=dev)
+    t8, rs = t8.contiguous(), rs.contiguous()
+    for _ in range(launches):
+        K.gemm_tcq(bits, t8, q4, s, rs, z, k)
+
+
+def _case_gemm(m, k, n, launches):
+    from . import kernels as K
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(12)
+    q = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev, generator=g)
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+    out = torch.empty(m, n, dtype=torch.int32, device=dev)
+    for _ in range(launches):
+        K.int_mm(q, w, out=out)
+
+
+def main(argv=None):
+    import argparse
+    ap = argparse.ArgumentParser(description='one kernel case for a profiler')
+    ap.add_argument('case', choices=['gemv', 'gemm'])
+    ap.add_argument('--m', type=int, default=4096)
+    ap.add_argument('--n', type=int, default=None)
+    ap.add_argument('--k', type=int, default=None)
+    ap.add_argument('--tokens', type=int, default=1)
+    ap.add_argument('--launches', type=int, default=4)
+    a = ap.parse_args(argv)
+    if a.case == 'gemv':
+        _case_gemv(a.n or 4096, a.k or 4096, a.tokens, a.launches)
+    else:
+        _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches)
+    torch.cuda.synchronize()
+    from . import kernels as K
+    err = K.device_error()
+    print('ok', a.case, 'device_error', err)
+    return 0 if err == 0 else 1
+
+
+if __name__ == '__main__':
+    raise SystemExit(main())
