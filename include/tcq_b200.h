@@ -169,6 +169,24 @@ size_t tcq_gemm_tcq_tc_workspace(int M, int N);
 int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z,
                     int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Policy glue around the quantized layers (no counterpart in the reference's kernels: its model code runs these as
+ * PyTorch ops, e.g. RMSNorm as float/pow/mean/rsqrt/mul/mul/cast). One launch per call, one block per token row.
+ *
+ * tcq_add_norm: h = x + y (BF16 add; written to h when h != NULL, y may be NULL for a plain norm), then
+ * kind 0 RMSNorm n = (h * rsqrt(sum(h^2) / D + eps)) * w, kind 1 LayerNorm n = ((h - mean) * rsqrt(var + eps)) * w + b
+ * (w, b (D,) of dtype wb_dtype, TCQ_DT_F32 or TCQ_DT_BF16; NULL = 1 / 0); with mod_scale / mod_shift (BF16 vectors, row stride ld_mod, one per group of
+ * mod_rows rows) n = n * (1 + mod_scale) + mod_shift (the DiT's AdaLN). out = BF16(n). x, y, h, out (M, D) BF16,
+ * D a multiple of 16, at most 32768. Row sums run in a fixed order: results are reproducible run to run. */
+int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* out, const void* w, const void* b, int wb_dtype,
+                 const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps, int kind, int M,
+                 int D, void* stream);
+
+/* Rotary position embedding, half-split form: for each of `heads` heads of width D in row r (position r % T) and
+ * j < D/2, (a, b) = (x[j], x[j + D/2]) -> (BF16(a cos - b sin), BF16(a sin + b cos)) in FP32 with one rounding per
+ * operation. x (rows, ldx) and out (rows, ldo) BF16 (out may equal x), cos / sin (T, D/2) FP32. */
+int tcq_rope(const uint16_t* x, uint16_t* out, const float* cos_t, const float* sin_t, int rows, int T, int heads, int D,
+             int ldx, int ldo, void* stream);
+
 /* Device error flags raised by bounded waits inside the kernels (1 = a pipeline wait expired and the kernel stopped
  * early). Synchronizes the current device. reset != 0 clears the flags. Returns -1 if the flags cannot be read. */
 int tcq_device_error(int reset);

@@ -13,6 +13,7 @@ LIB_PATH = Path(os.environ.get('TCQ_B200_LIB', _PKG / 'libtcq_b200.so'))
 P = ctypes.c_void_p
 I = ctypes.c_int
 SZ = ctypes.c_size_t
+F = ctypes.c_float
 
 # name -> argument types (every function returns int, except where noted)
 SIGNATURES = {
@@ -39,6 +40,8 @@ SIGNATURES = {
     'tcq_gemm_tcq_tc': [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P],
     'tcq_int_mm': [P, P, P, I, I, I, P],
     'tcq_int8_gemm': [P, P, P, P, P, I, I, I, I, P],
+    'tcq_add_norm': [P, P, P, P, P, P, I, P, P, I, I, F, I, I, I, P],
+    'tcq_rope': [P, P, P, P, I, I, I, I, I, I, P],
     'tcq_device_error': [I],
 }
 RESTYPES = {'tcq_status_string': ctypes.c_char_p, 'tcq_gemm_tcq_workspace': SZ, 'tcq_gemm_tcq_tc_workspace': SZ, 'tcq_gemm_tcq_noalloc_max_elements': SZ}

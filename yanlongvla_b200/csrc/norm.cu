@@ -1,0 +1,202 @@
+// Row kernels for the policy's glue around the quantized layers: residual add + RMSNorm / LayerNorm (+ the DiT's
+// AdaLN modulation) in one pass, and the rotary position embedding.
+//
+// One thread block per token row. A thread owns 16-element chunks c = threadIdx.x + k * blockDim.x of the row and
+// keeps them in registers; row sums are taken in a fixed order (each thread's elements in index order, then a
+// butterfly over the warp, then the warps' sums in warp order), so a row's result does not depend on timing.
+// The policy runs every runtime (the PyTorch reference runtime included) through these kernels, so the runtimes
+// agree bit for bit; tests compare them with a PyTorch FP32 restatement within BF16 rounding.
+#include "tcq_common.cuh"
+
+namespace {
+
+constexpr int kMaxChunks = 4;      // 16-element chunks per thread: rows up to 16 * 4 * 512 = 32768 wide
+
+__device__ __forceinline__ float bf16_round(float f) { return bf2f(f2bf(f)); }
+
+// Sum over the block in a fixed order; every thread receives the same value. `red` holds one float per warp.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();                               // red may still be read by a previous reduction
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+    const int warps = (blockDim.x + 31) >> 5;
+    for (int i = 0; i < warps; ++i) t += red[i];
+    return t;
+}
+
+__device__ __forceinline__ void load_bf16x16(const u16* p, float* v) {
+    const uint4* u = reinterpret_cast<const uint4*>(p);
+    const uint4 a = __ldg(u), b = __ldg(u + 1);
+    const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = bf2f((u16)(w[i] & 0xffffu));
+        v[2 * i + 1] = bf2f((u16)(w[i] >> 16));
+    }
+}
+
+__device__ __forceinline__ void store_bf16x16(u16* p, const float* v) {
+    u32 w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = (u32)f2bf(v[2 * i]) | ((u32)f2bf(v[2 * i + 1]) << 16);
+    uint4* u = reinterpret_cast<uint4*>(p);
+    u[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    u[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// Element j of an FP32 or BF16 parameter vector.
+template <bool WBF16>
+__device__ __forceinline__ float ldp(const void* p, int j) {
+    if (WBF16) return bf2f(__ldg(reinterpret_cast<const u16*>(p) + j));
+    return __ldg(reinterpret_cast<const float*>(p) + j);
+}
+
+// h = x (+ y, rounded to BF16 as a BF16 tensor add does); written to hout when given.
+// KIND 0 (RMSNorm):   n = (h * r) * w,                    r = rsqrt(sum(h^2) / D + eps)
+// KIND 1 (LayerNorm): n = ((h - mu) * r) * w + b,         mu = sum(h) / D, r = rsqrt(sum((h - mu)^2) / D + eps)
+// w / b optional (NULL = 1 / 0), FP32 or (WBF16) BF16. Modulation (mscale != NULL): n = n * (1 + mscale[g]) +
+// mshift[g] for the row group g = row / mod_rows (rows of one sample), mscale / mshift BF16 vectors with row stride
+// ld_mod. out = BF16(n).
+template <int KIND, bool WBF16>
+__global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
+                                                 u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
+                                                 const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
+                                                 int ld_mod, float eps, int D) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int row = blockIdx.x, nch = D >> 4;
+    const size_t base = (size_t)row * D;
+    float v[kMaxChunks][16];
+    float part = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+            load_bf16x16(x + base + 16 * c, v[k]);
+            if (y) {
+                float t[16];
+                load_bf16x16(y + base + 16 * c, t);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[k][i] = bf16_round(v[k][i] + t[i]);
+                if (hout) store_bf16x16(hout + base + 16 * c, v[k]);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) part += KIND == 0 ? v[k][i] * v[k][i] : v[k][i];
+        }
+    }
+    const float tot = block_sum(part, red);
+    float mu = 0.f, r;
+    if (KIND == 0) {
+        r = rsqrtf(tot / (float)D + eps);
+    } else {
+        mu = tot / (float)D;
+        float p2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxChunks; ++k) {
+            const int c = threadIdx.x + k * blockDim.x;
+            if (c < nch) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float d = v[k][i] - mu;
+                    p2 += d * d;
+                }
+            }
+        }
+        r = rsqrtf(block_sum(p2, red) / (float)D + eps);
+    }
+    const u16* ms = mscale ? mscale + (size_t)(row / mod_rows) * ld_mod : nullptr;
+    const u16* mh = mscale ? mshift + (size_t)(row / mod_rows) * ld_mod : nullptr;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+            float o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int j = 16 * c + i;
+                float t = KIND == 0 ? v[k][i] * r : (v[k][i] - mu) * r;
+                if (w) t = t * ldp<WBF16>(w, j);
+                if (b) t = t + ldp<WBF16>(b, j);
+                if (ms) t = t * (1.f + bf2f(__ldg(ms + j))) + bf2f(__ldg(mh + j));
+                o[i] = t;
+            }
+            store_bf16x16(nout + base + 16 * c, o);
+        }
+    }
+}
+
+// Rotary embedding, half-split form, on rows of `heads` heads of width D (row r is position r % T):
+// out[a] = BF16(a * cos - b * sin), out[b] = BF16(a * sin + b * cos) for the pair (a, b) = (x[j], x[j + D/2]) of each
+// head, FP32 arithmetic in that order. cos / sin: (T, D / 2) FP32.
+__global__ void __launch_bounds__(256) k_rope(const u16* __restrict__ x, u16* __restrict__ out, const float* __restrict__ cs,
+                                              const float* __restrict__ sn, int T, int heads, int D, int ldx, int ldo) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int row = blockIdx.x, half = D >> 1, t = row % T;
+    const u16* xr = x + (size_t)row * ldx;
+    u16* orow = out + (size_t)row * ldo;
+    for (int i = threadIdx.x; i < heads * half; i += blockDim.x) {
+        const int h = i / half, j = i - h * half;
+        const float a = bf2f(xr[h * D + j]), bb = bf2f(xr[h * D + half + j]);
+        const float c = __ldg(cs + (size_t)t * half + j), s = __ldg(sn + (size_t)t * half + j);
+        const float p = a * c, q = bb * s, u = a * s, v = bb * c;
+        orow[h * D + j] = f2bf(p - q);
+        orow[h * D + half + j] = f2bf(u + v);
+    }
+}
+
+int norm_threads(int D) {
+    int t = ((D >> 4) + 31) & ~31;
+    if (t < 32) t = 32;
+    if (t > 512) t = 512;
+    return t;
+}
+
+template <class Kern, class... Args>
+int launch_rows(Kern kern, int rows, int threads, void* stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* out, const void* w, const void* b, int wb_dtype,
+                 const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps, int kind, int M,
+                 int D, void* stream) {
+    if (!x || !out || (h && !y) || (!mod_scale != !mod_shift)) return TCQ_ERR_ARG;
+    if (kind != 0 && kind != 1) return TCQ_ERR_ARG;
+    if (wb_dtype != TCQ_DT_F32 && wb_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
+    if (M <= 0 || D <= 0 || (D & 15) || D > 16 * kMaxChunks * 512) return TCQ_ERR_SHAPE;
+    if (mod_scale && (mod_rows <= 0 || ld_mod < D)) return TCQ_ERR_ARG;
+    if (!tcq_aligned(x, 16) || !tcq_aligned(out, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)))
+        return TCQ_ERR_ALIGN;
+    const int T = norm_threads(D);
+    const bool wb = wb_dtype == TCQ_DT_BF16;
+    auto kern = kind == 0 ? (wb ? k_addnorm<0, true> : k_addnorm<0, false>) : (wb ? k_addnorm<1, true> : k_addnorm<1, false>);
+    return launch_rows(kern, M, T, stream, (const u16*)x, (const u16*)y, (u16*)h, (u16*)out, w, b, (const u16*)mod_scale,
+                       (const u16*)mod_shift, mod_rows, ld_mod, eps, D);
+}
+
+int tcq_rope(const uint16_t* x, uint16_t* out, const float* cos_t, const float* sin_t, int rows, int T, int heads, int D,
+             int ldx, int ldo, void* stream) {
+    if (!x || !out || !cos_t || !sin_t) return TCQ_ERR_ARG;
+    if (rows <= 0 || T <= 0 || heads <= 0 || D <= 0 || (D & 1) || ldx < heads * D || ldo < heads * D) return TCQ_ERR_SHAPE;
+    return launch_rows(k_rope, rows, 256, stream, (const u16*)x, (u16*)out, cos_t, sin_t, T, heads, D, ldx, ldo);
+}
+
+}  // extern "C"

@@ -204,6 +204,67 @@ def rotate(x, signs, inverse=False, out_dtype=torch.float32, out=None):
     return y.view(*shape)
 
 
+# ------------------------------------------------------------------------------------------------ policy glue
+def add_norm(x, y=None, weight=None, bias=None, eps=1e-6, kind='rms', h_out=None, out=None, mod=None, mod_rows=1):
+    """Residual add + RMSNorm / LayerNorm in one launch (tcq_add_norm). x, y (..., D) BF16; returns (h, n) with
+    h = x + y (x itself when y is None; written to h_out when given, which may be x) and n = norm(h) in BF16.
+    kind 'rms': n = (h * rsqrt(mean(h^2) + eps)) * weight; kind 'ln': n = ((h - mean) * rsqrt(var + eps)) * weight + bias
+    (weight / bias FP32, None = 1 / 0). mod = (scale, shift) BF16 (G, D) views, one row per group of mod_rows rows:
+    n = n * (1 + scale) + shift."""
+    shape = x.shape
+    D = shape[-1]
+    x2 = x.reshape(-1, D)
+    M = x2.shape[0]
+    y2 = None if y is None else y.reshape(-1, D)
+    for t in (x2, y2):
+        if t is not None and (t.dtype != torch.bfloat16 or not t.is_contiguous()):
+            raise TypeError('add_norm: x and y must be contiguous BF16')
+    h = x2 if y2 is None else (torch.empty_like(x2) if h_out is None else h_out.view(M, D))
+    n = torch.empty_like(x2) if out is None else out.view(M, D)
+    ms = mh = None
+    ld = 0
+    if mod is not None:
+        ms, mh = mod
+        if ms.dtype != torch.bfloat16 or mh.dtype != torch.bfloat16 or ms.stride(-1) != 1 or ms.stride(0) != mh.stride(0):
+            raise TypeError('add_norm: mod must be BF16 (G, D) views with unit inner stride')
+        ld = ms.stride(0) if ms.dim() > 1 else D
+    _cuda(x2, n, *(t for t in (y2, weight, bias) if t is not None))
+    if ms is not None and not (ms.is_cuda and mh.is_cuda and ms.shape[-1] == D and mh.shape[-1] == D):
+        raise TcqError('add_norm: mod must be CUDA (G, D) tensors')
+    if h.shape != x2.shape or n.shape != x2.shape or (y2 is not None and y2.shape != x2.shape):
+        raise TcqError('add_norm: x, y and the outputs must have the same shape')
+    wdt = [t.dtype for t in (weight, bias) if t is not None]
+    if any(d != wdt[0] for d in wdt) or (wdt and wdt[0] not in (torch.float32, torch.bfloat16)):
+        raise TcqError(f'add_norm: weight / bias must both be float32 or both bfloat16, got {wdt}')
+    for t in (weight, bias):
+        if t is not None and t.numel() != D:
+            raise TcqError(f'add_norm: weight / bias must have {D} elements')
+    check(lib.tcq_add_norm(_p(x2), None if y2 is None else _p(y2), None if y2 is None else _p(h), _p(n),
+                           None if weight is None else _p(weight), None if bias is None else _p(bias),
+                           _DT[wdt[0]] if wdt else DT_F32,
+                           None if ms is None else _p(ms), None if mh is None else _p(mh), int(mod_rows), int(ld),
+                           float(eps), {'rms': 0, 'ln': 1}[kind], M, D, _stream()), 'tcq_add_norm')
+    _count('add_norm')
+    return h.view(shape), n.view(shape)
+
+
+def rope(x, cos, sin, heads, out=None):
+    """Rotary embedding (half-split form) on x (B, T, heads * D) BF16 with cos / sin (T, D/2) FP32 tables."""
+    B, T, W = x.shape
+    D = W // heads
+    if x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.stride(0) != T * x.stride(1):
+        raise TypeError('rope: x must be BF16 with contiguous rows')
+    y = torch.empty(B, T, W, dtype=torch.bfloat16, device=x.device) if out is None else out
+    _cuda(x, y, cos, sin)
+    if W % heads or D % 2 or y.shape != x.shape or y.dtype != torch.bfloat16:
+        raise TcqError('rope: x (B, T, heads * D) with even D, out of the same shape, BF16')
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32 or cos.shape != (T, D // 2) or sin.shape != (T, D // 2):
+        raise TcqError(f'rope: cos / sin must be float32 ({T}, {D // 2})')
+    check(lib.tcq_rope(_p(x), _p(y), _p(cos), _p(sin), B * T, T, heads, D, x.stride(1), y.stride(1), _stream()), 'tcq_rope')
+    _count('rope')
+    return y
+
+
 # ------------------------------------------------------------------------------------------------ trellis weights
 def decode(bits, t8, out):
     """bits (m/16 * n/16, 32) int16/uint16 words, t8 (512, 2) int8 -> out (m, n) int8."""

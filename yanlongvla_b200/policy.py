@@ -98,7 +98,8 @@ class W8A8Linear(torch.nn.Module):
 
 
 def _attention(q, k, v, heads, kv_heads=None, causal=False):
-    """q (B, Tq, H*D), k / v (B, Tk, Hk*D) BF16 -> (B, Tq, H*D)."""
+    """q (B, Tq, H*D), k / v (B, Tk, Hk*D) BF16 -> (B, Tq, H*D). Grouped-query heads share their K / V inside the
+    attention kernel (no repeated copies)."""
     B, Tq, _ = q.shape
     Tk = k.shape[1]
     kv_heads = kv_heads or heads
@@ -106,42 +107,53 @@ def _attention(q, k, v, heads, kv_heads=None, causal=False):
     q = q.view(B, Tq, heads, D).transpose(1, 2)
     k = k.view(B, Tk, kv_heads, D).transpose(1, 2)
     v = v.view(B, Tk, kv_heads, D).transpose(1, 2)
-    if kv_heads != heads:
-        k = k.repeat_interleave(heads // kv_heads, dim=1)
-        v = v.repeat_interleave(heads // kv_heads, dim=1)
-    o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=kv_heads != heads)
     return o.transpose(1, 2).reshape(B, Tq, heads * D)
 
 
-def _rope(x, heads, pos):
-    """Rotary position embedding on (B, T, heads * D) BF16 (half-split form)."""
-    B, T, _ = x.shape
-    D = x.shape[-1] // heads
-    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=x.device, dtype=torch.float32) / D))
-    ang = pos[:, None].float() * inv[None, :]
-    cos, sin = ang.cos()[None, :, None, :], ang.sin()[None, :, None, :]
-    xh = x.view(B, T, heads, D).float()
-    a, b = xh[..., :D // 2], xh[..., D // 2:]
-    return torch.cat((a * cos - b * sin, a * sin + b * cos), -1).to(x.dtype).view(B, T, heads * D)
+def rope_tables(T, D, device):
+    """cos / sin (T, D/2) FP32 of the half-split rotary embedding at positions 0..T-1 (computed once per forward)."""
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+    ang = torch.arange(T, device=device).float()[:, None] * inv[None, :]
+    return ang.cos().contiguous(), ang.sin().contiguous()
 
 
 class RMSNorm(torch.nn.Module):
+    """RMSNorm with FP32 weight, eps 1e-6; `forward(x, delta)` first adds the pending residual delta (one kernel,
+    kernels.add_norm) and returns (x + delta, norm(x + delta))."""
     def __init__(self, d):
         super().__init__()
         self.weight = torch.nn.Parameter(torch.ones(d))
 
-    def forward(self, x):
-        h = x.float()
-        return (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6) * self.weight).to(x.dtype)
+    def forward(self, x, delta=None):
+        return K.add_norm(x, delta, self.weight, None, 1e-6, 'rms')
 
 
+class LayerNorm(torch.nn.Module):
+    """LayerNorm (eps 1e-5 as torch's default, FP32 weight / bias when affine) through kernels.add_norm;
+    `forward(x, delta, mod)` as RMSNorm's, with the optional AdaLN modulation (scale, shift) per sample."""
+    def __init__(self, d, elementwise_affine=True, eps=1e-5):
+        super().__init__()
+        self.eps = eps
+        if elementwise_affine:
+            self.weight = torch.nn.Parameter(torch.ones(d))
+            self.bias = torch.nn.Parameter(torch.zeros(d))
+        else:
+            self.weight = self.bias = None
+
+    def forward(self, x, delta=None, mod=None, mod_rows=1):
+        return K.add_norm(x, delta, self.weight, self.bias, self.eps, 'ln', mod=mod, mod_rows=mod_rows)
+
+
+# Blocks take the residual stream x and the pending residual delta of the previous block (None for the first): the
+# add is folded into the block's first norm. They return (x, delta) for the next block.
 class VitBlock(torch.nn.Module):
     def __init__(self, c):
         super().__init__()
         d = c.vit_hidden
         self.heads = c.vit_heads
-        self.layer_norm1 = torch.nn.LayerNorm(d)
-        self.layer_norm2 = torch.nn.LayerNorm(d)
+        self.layer_norm1 = LayerNorm(d)
+        self.layer_norm2 = LayerNorm(d)
         self.self_attn = torch.nn.Module()
         for n in ('q_proj', 'k_proj', 'v_proj', 'out_proj'):
             setattr(self.self_attn, n, LinearSlot(d, d, bias=True))
@@ -149,13 +161,12 @@ class VitBlock(torch.nn.Module):
         self.mlp.fc1 = LinearSlot(d, c.vit_mlp, bias=True)
         self.mlp.fc2 = LinearSlot(c.vit_mlp, d, bias=True)
 
-    def forward(self, x):
-        h = self.layer_norm1(x)
+    def forward(self, x, delta=None):
+        x, h = self.layer_norm1(x, delta)
         a = self.self_attn
         o = _attention(a.q_proj(h), a.k_proj(h), a.v_proj(h), self.heads)
-        x = x + a.out_proj(o)
-        h = self.layer_norm2(x)
-        return x + self.mlp.fc2(F.gelu(self.mlp.fc1(h), approximate='tanh'))
+        x, h = self.layer_norm2(x, a.out_proj(o))
+        return x, self.mlp.fc2(F.gelu(self.mlp.fc1(h), approximate='tanh'))
 
 
 class LlmBlock(torch.nn.Module):
@@ -177,13 +188,15 @@ class LlmBlock(torch.nn.Module):
         self.mlp.down_proj = LinearSlot(c.llm_ffn, d)
         self.mlp.forward = lambda x: self.mlp.down_proj(F.silu(self.mlp.gate_proj(x)) * self.mlp.up_proj(x))
 
-    def forward(self, x, pos):
-        h = self.input_layernorm(x)
+    def forward(self, x, delta, rope):
+        x, h = self.input_layernorm(x, delta)
         a = self.self_attn
         q, k, v = a.q_proj(h), a.k_proj(h), a.v_proj(h)
-        o = _attention(_rope(q, self.heads, pos), _rope(k, self.kv_heads, pos), v, self.heads, self.kv_heads, causal=True)
-        x = x + a.o_proj(o)
-        return x + self.mlp(self.post_attention_layernorm(x))
+        cos, sin = rope
+        q, k = K.rope(q, cos, sin, self.heads, out=q), K.rope(k, cos, sin, self.kv_heads, out=k)
+        o = _attention(q, k, v, self.heads, self.kv_heads, causal=True)
+        x, h = self.post_attention_layernorm(x, a.o_proj(o))
+        return x, self.mlp(h)
 
 
 class DitBlock(torch.nn.Module):
@@ -191,8 +204,8 @@ class DitBlock(torch.nn.Module):
         super().__init__()
         d = c.dit_hidden
         self.heads, self.cross = c.dit_heads, cross
-        self.norm1 = torch.nn.LayerNorm(d, elementwise_affine=False)
-        self.norm3 = torch.nn.LayerNorm(d)
+        self.norm1 = LayerNorm(d, elementwise_affine=False, eps=1e-6)
+        self.norm3 = LayerNorm(d)
         self.adaln = LinearSlot(d, 2 * d)                      # timestep -> (scale, shift)
         self.attn1 = torch.nn.Module()
         self.attn1.q_proj = LinearSlot(d, d)
@@ -208,18 +221,18 @@ class DitBlock(torch.nn.Module):
         """Cross-attention keys / values of the backbone features: computed once per action chunk."""
         return self.attn1.k_proj(feats), self.attn1.v_proj(feats)
 
-    def forward(self, x, temb, kv=None):
-        mod = self.adaln(F.silu(temb))                        # (B, 1, 2d)
-        scale, shift = mod.chunk(2, dim=-1)
-        h = (self.norm1(x) * (1 + scale) + shift).to(x.dtype)
+    def forward(self, x, delta, silu_temb, kv=None):
+        d = x.shape[-1]
+        mod = self.adaln(silu_temb)                           # (B, 1, 2d): AdaLN scale, shift
+        x, h = self.norm1(x, delta, mod=(mod[:, 0, :d], mod[:, 0, d:]), mod_rows=x.shape[1])
         a = self.attn1
         if self.cross:
             k, v = kv
             o = _attention(a.q_proj(h), k, v, self.heads)
         else:
             o = _attention(a.q_proj(h), a.k_proj(h), a.v_proj(h), self.heads)
-        x = x + a.o_proj(o)
-        return x + self.ff(self.norm3(x))
+        x, h = self.norm3(x, a.o_proj(o))
+        return x, self.ff(h)
 
 
 class GrootStylePolicy(torch.nn.Module):
@@ -230,8 +243,8 @@ class GrootStylePolicy(torch.nn.Module):
         self.patch_embed = torch.nn.Linear(3 * c.patch * c.patch, dv)
         self.pos_embed = torch.nn.Parameter(torch.zeros(c.patches, dv))
         self.vit = torch.nn.ModuleList([VitBlock(c) for _ in range(c.vit_layers)])
-        self.vit_norm = torch.nn.LayerNorm(dv)
-        self.proj_norm = torch.nn.LayerNorm(dv * c.shuffle ** 2)
+        self.vit_norm = LayerNorm(dv)
+        self.proj_norm = LayerNorm(dv * c.shuffle ** 2)
         self.proj1 = torch.nn.Linear(dv * c.shuffle ** 2, dl)
         self.proj2 = torch.nn.Linear(dl, dl)
         self.embed_tokens = torch.nn.Embedding(c.vocab, dl)
@@ -243,7 +256,7 @@ class GrootStylePolicy(torch.nn.Module):
         self.time1 = torch.nn.Linear(256, dd)
         self.time2 = torch.nn.Linear(dd, dd)
         self.dit = torch.nn.ModuleList([DitBlock(c, cross=(i % 2 == 0)) for i in range(c.dit_layers)])
-        self.out_norm = torch.nn.LayerNorm(dd)
+        self.out_norm = LayerNorm(dd)
         self.proj_out = torch.nn.Linear(dd, c.action_dim)
 
     # ---------------------------------------------------------------------------------------------------- stages
@@ -255,21 +268,23 @@ class GrootStylePolicy(torch.nn.Module):
         g = c.image // c.patch
         x = x.view(B * c.cameras, g, c.patch, g, c.patch, 3).permute(0, 1, 3, 2, 4, 5).reshape(B * c.cameras, g * g, -1)
         h = self.patch_embed(x) + self.pos_embed.to(torch.bfloat16)
+        d = None
         for blk in self.vit:
-            h = blk(h)
-        h = self.vit_norm(h)
+            h, d = blk(h, d)
+        _, h = self.vit_norm(h, d)
         s = c.shuffle
         h = h.view(B * c.cameras, g // s, s, g // s, s, -1).permute(0, 1, 3, 2, 4, 5).reshape(B * c.cameras, (g // s) ** 2, -1)
-        img = self.proj2(F.gelu(self.proj1(self.proj_norm(h)), approximate='tanh'))
+        img = self.proj2(F.gelu(self.proj1(self.proj_norm(h)[1]), approximate='tanh'))
         img = img.view(B, c.cameras * c.image_tokens, -1)
         return torch.cat((img, self.embed_tokens(lang_ids)), 1)
 
     def backbone(self, prefix):
-        pos = torch.arange(prefix.shape[1], device=prefix.device)
-        x = prefix
+        c = self.c
+        rope = rope_tables(prefix.shape[1], c.llm_hidden // c.llm_heads, prefix.device)
+        x, d = prefix, None
         for blk in self.llm:
-            x = blk(x, pos)
-        return self.llm_norm(x)
+            x, d = blk(x, d, rope)
+        return self.llm_norm(x, d)[1]
 
     def timestep(self, t, B, device):
         half = 128
@@ -290,9 +305,10 @@ class GrootStylePolicy(torch.nn.Module):
         for k in range(c.flow_steps):
             temb = self.timestep(ts[k], B, feats.device)
             x = torch.cat((st, self.action_enc(a.to(torch.bfloat16)) + temb), 1)
+            silu_temb, d = F.silu(temb), None
             for blk, kv in zip(self.dit, kvs):
-                x = blk(x, temb, kv)
-            v = self.proj_out(self.out_norm(x[:, 1:]))
+                x, d = blk(x, d, silu_temb, kv)
+            v = self.proj_out(self.out_norm(x, d)[1][:, 1:])
             a = a + dt * v.float()
         return a
 
