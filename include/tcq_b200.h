@@ -181,6 +181,18 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
                  const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps, int kind, int M,
                  int D, void* stream);
 
+/* Fused chain across a residual block boundary: one layer's post-rotation fused with the next layer's pre-rotation
+ * through the residual add and norm between them (no single counterpart in the reference, which runs kernels.post,
+ * the model's PyTorch add + norm and kernels.pre, kernels.py:602-628): per token row
+ *   y = tcq_post(acc, ...) (acc != NULL; acc_dtype I32 with s / rs, or F32 z already scaled) or y = the BF16 tensor y,
+ *   h = BF16(x + y) -> h (h = x without y), n = the norm of tcq_add_norm (same arguments, same arithmetic and order)
+ *   -> n when n != NULL, and with su != NULL q / q4 / scale = tcq_pre(BF16(n), su) of the next layer.
+ * Each stage is bit-identical to the separate entry point. x, y, h, n (M, N) BF16; acc (M, lda) from column col0. */
+int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias, int lda,
+              int col0, const uint16_t* y, const uint16_t* x, uint16_t* h, uint16_t* n, const void* w, const void* b,
+              int wb_dtype, const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps,
+              int kind, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int ldq, int M, int N, void* stream);
+
 /* Rotary position embedding, half-split form: for each of `heads` heads of width D in row r (position r % T) and
  * j < D/2, (a, b) = (x[j], x[j + D/2]) -> (BF16(a cos - b sin), BF16(a sin + b cos)) in FP32 with one rounding per
  * operation. x (rows, ldx) and out (rows, ldo) BF16 (out may equal x), cos / sin (T, D/2) FP32. */

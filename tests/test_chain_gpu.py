@@ -1,0 +1,100 @@
+"""tcq_chain (post -> residual add -> norm -> pre in one launch) against the three separate entry points.
+
+Every stage of the chain is specified as the separate kernel's arithmetic (kernels.post, kernels.add_norm with the
+same thread count and sum order, kernels.pre), so the fused outputs must equal the decomposition bit for bit: the new
+residual h, the norm output n, the next layer's INT8 activations (q and q4 layouts) and their scales."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip('no CUDA device')
+    from yanlongvla_b200 import kernels
+    return kernels
+
+
+def _signs(n, g):
+    return (torch.randint(0, 2, (n,), device='cuda', generator=g) * 2 - 1).to(torch.int8)
+
+
+def _case(M, N, at, g, lda_extra=0):
+    lda = N + lda_extra
+    if at == 'i32':
+        acc = torch.randint(-2 ** 20, 2 ** 20, (M, lda), dtype=torch.int32, device='cuda', generator=g)
+        s = torch.rand(M, device='cuda', generator=g) * 1e-3 + 1e-4
+        rs = torch.rand(N, device='cuda', generator=g) * 1e-2 + 1e-3
+    else:
+        acc = torch.randn(M, lda, device='cuda', generator=g) * 2
+        s = rs = None
+    sv = _signs(N, g)
+    return acc, s, rs, sv
+
+
+@pytest.mark.parametrize('M,N', [(1, 2048), (3, 1536), (17, 1536), (160, 2048), (40, 1152), (9, 6144)])
+@pytest.mark.parametrize('at', ['i32', 'f32'])
+@pytest.mark.parametrize('kind', ['rms', 'ln'])
+def test_chain_equals_post_addnorm_pre(K, M, N, at, kind):
+    g = torch.Generator(device='cuda').manual_seed(M * 131 + N + (7 if at == 'f32' else 0) + (3 if kind == 'ln' else 0))
+    col0 = 16 if at == 'i32' else 0
+    acc, s, rs, sv = _case(M, N, at, g, lda_extra=col0 + 32)
+    bias = torch.randn(N, device='cuda', generator=g) * 0.1 if kind == 'ln' else None
+    x = torch.randn(M, N, device='cuda', generator=g).bfloat16()
+    w = (torch.rand(N, device='cuda', generator=g) + 0.5).bfloat16()
+    nb = (torch.randn(N, device='cuda', generator=g) * 0.1).bfloat16() if kind == 'ln' else None
+    su = _signs(N, g)
+    eps = 1e-6 if kind == 'rms' else 1e-5
+    # decomposition: three launches
+    y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+    K.post(acc, s, None if rs is None else rs, sv, bias, y, col0=col0)
+    h_ref, n_ref = K.add_norm(x, y, w, nb, eps, kind)
+    q_ref = torch.empty(M, N, dtype=torch.int8, device='cuda')
+    q4_ref = torch.empty(N // 4, M + 3, dtype=torch.int32, device='cuda')
+    sc_ref = torch.empty(M, device='cuda')
+    K.pre(n_ref, su, q=q_ref, q4=q4_ref, scale=sc_ref)
+    # fused: one launch
+    q = torch.empty_like(q_ref)
+    q4 = torch.zeros_like(q4_ref)
+    sc = torch.empty_like(sc_ref)
+    q4_ref[:, M:] = 0
+    h, n = K.chain(x, kind, w, nb, eps, acc=acc, s=s, rs=rs, sv=sv, bias=bias, col0=col0, su=su, q=q, q4=q4, scale=sc)
+    assert torch.equal(h, h_ref)
+    assert torch.equal(n, n_ref)
+    assert torch.equal(q, q_ref) and torch.equal(q4, q4_ref) and torch.equal(sc, sc_ref)
+
+
+def test_chain_with_tensor_add_and_modulation(K):
+    """y from a BF16 tensor (a producer whose post already ran) and the DiT's AdaLN modulation, pre to q only."""
+    B, T, N = 2, 17, 1536
+    g = torch.Generator(device='cuda').manual_seed(21)
+    x = torch.randn(B * T, N, device='cuda', generator=g).bfloat16()
+    y = torch.randn(B * T, N, device='cuda', generator=g).bfloat16()
+    mod = (torch.randn(B, 1, 2 * N, device='cuda', generator=g) * 0.3).bfloat16()
+    ms, mh = mod[:, 0, :N], mod[:, 0, N:]
+    su = _signs(N, g)
+    h_ref, n_ref = K.add_norm(x, y, None, None, 1e-6, 'ln', mod=(ms, mh), mod_rows=T)
+    q_ref = torch.empty(B * T, N, dtype=torch.int8, device='cuda')
+    sc_ref = torch.empty(B * T, device='cuda')
+    K.pre(n_ref, su, q=q_ref, scale=sc_ref)
+    q = torch.empty_like(q_ref)
+    sc = torch.empty_like(sc_ref)
+    h, n = K.chain(x, 'ln', None, None, 1e-6, y=y, mod=(ms, mh), mod_rows=T, su=su, q=q, scale=sc, want_n=False)
+    assert n is None and torch.equal(h, h_ref) and torch.equal(q, q_ref) and torch.equal(sc, sc_ref)
+
+
+def test_chain_norm_pre_without_add(K):
+    """The first block of a stack: no pending residual, norm + pre of x itself."""
+    g = torch.Generator(device='cuda').manual_seed(22)
+    x = torch.randn(160, 2048, device='cuda', generator=g).bfloat16()
+    w = torch.rand(2048, device='cuda', generator=g).bfloat16() + 0.5
+    su = _signs(2048, g)
+    _, n_ref = K.add_norm(x, None, w, None, 1e-6, 'rms')
+    q_ref = torch.empty(160, 2048, dtype=torch.int8, device='cuda')
+    sc_ref = torch.empty(160, device='cuda')
+    K.pre(n_ref, su, q=q_ref, scale=sc_ref)
+    q, sc = torch.empty_like(q_ref), torch.empty_like(sc_ref)
+    h, n = K.chain(x, 'rms', w, None, 1e-6, su=su, q=q, scale=sc)
+    assert h.data_ptr() == x.data_ptr() and torch.equal(n, n_ref) and torch.equal(q, q_ref) and torch.equal(sc, sc_ref)

@@ -6,60 +6,14 @@
 // butterfly over the warp, then the warps' sums in warp order), so a row's result does not depend on timing.
 // The policy runs every runtime (the PyTorch reference runtime included) through these kernels, so the runtimes
 // agree bit for bit; tests compare them with a PyTorch FP32 restatement within BF16 rounding.
-#include "tcq_common.cuh"
+#include "rownorm.cuh"
 
 namespace {
 
-constexpr int kMaxChunks = 4;      // 16-element chunks per thread: rows up to 16 * 4 * 512 = 32768 wide
+using namespace tcq;
 
-__device__ __forceinline__ float bf16_round(float f) { return bf2f(f2bf(f)); }
-
-// Sum over the block in a fixed order; every thread receives the same value. `red` holds one float per warp.
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    __syncthreads();                               // red may still be read by a previous reduction
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float t = 0.f;
-    const int warps = (blockDim.x + 31) >> 5;
-    for (int i = 0; i < warps; ++i) t += red[i];
-    return t;
-}
-
-__device__ __forceinline__ void load_bf16x16(const u16* p, float* v) {
-    const uint4* u = reinterpret_cast<const uint4*>(p);
-    const uint4 a = __ldg(u), b = __ldg(u + 1);
-    const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        v[2 * i] = bf2f((u16)(w[i] & 0xffffu));
-        v[2 * i + 1] = bf2f((u16)(w[i] >> 16));
-    }
-}
-
-__device__ __forceinline__ void store_bf16x16(u16* p, const float* v) {
-    u32 w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w[i] = (u32)f2bf(v[2 * i]) | ((u32)f2bf(v[2 * i + 1]) << 16);
-    uint4* u = reinterpret_cast<uint4*>(p);
-    u[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    u[1] = make_uint4(w[4], w[5], w[6], w[7]);
-}
-
-// Element j of an FP32 or BF16 parameter vector.
-template <bool WBF16>
-__device__ __forceinline__ float ldp(const void* p, int j) {
-    if (WBF16) return bf2f(__ldg(reinterpret_cast<const u16*>(p) + j));
-    return __ldg(reinterpret_cast<const float*>(p) + j);
-}
-
-// h = x (+ y, rounded to BF16 as a BF16 tensor add does); written to hout when given.
-// KIND 0 (RMSNorm):   n = (h * r) * w,                    r = rsqrt(sum(h^2) / D + eps)
-// KIND 1 (LayerNorm): n = ((h - mu) * r) * w + b,         mu = sum(h) / D, r = rsqrt(sum((h - mu)^2) / D + eps)
-// w / b optional (NULL = 1 / 0), FP32 or (WBF16) BF16. Modulation (mscale != NULL): n = n * (1 + mscale[g]) +
-// mshift[g] for the row group g = row / mod_rows (rows of one sample), mscale / mshift BF16 vectors with row stride
-// ld_mod. out = BF16(n).
+// h = x (+ y, rounded to BF16 as a BF16 tensor add does); written to hout when given; out = BF16(norm_chunks(h)).
+// Modulation vectors: row group g = row / mod_rows (rows of one sample), row stride ld_mod.
 template <int KIND, bool WBF16>
 __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
                                                  u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
@@ -70,10 +24,9 @@ __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, cons
     pdl_wait();
     const int row = blockIdx.x, nch = D >> 4;
     const size_t base = (size_t)row * D;
-    float v[kMaxChunks][16];
-    float part = 0.f;
+    float v[kNormMaxChunks][16];
 #pragma unroll
-    for (int k = 0; k < kMaxChunks; ++k) {
+    for (int k = 0; k < kNormMaxChunks; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
             load_bf16x16(x + base + 16 * c, v[k]);
@@ -84,48 +37,15 @@ __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, cons
                 for (int i = 0; i < 16; ++i) v[k][i] = bf16_round(v[k][i] + t[i]);
                 if (hout) store_bf16x16(hout + base + 16 * c, v[k]);
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) part += KIND == 0 ? v[k][i] * v[k][i] : v[k][i];
         }
-    }
-    const float tot = block_sum(part, red);
-    float mu = 0.f, r;
-    if (KIND == 0) {
-        r = rsqrtf(tot / (float)D + eps);
-    } else {
-        mu = tot / (float)D;
-        float p2 = 0.f;
-#pragma unroll
-        for (int k = 0; k < kMaxChunks; ++k) {
-            const int c = threadIdx.x + k * blockDim.x;
-            if (c < nch) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float d = v[k][i] - mu;
-                    p2 += d * d;
-                }
-            }
-        }
-        r = rsqrtf(block_sum(p2, red) / (float)D + eps);
     }
     const u16* ms = mscale ? mscale + (size_t)(row / mod_rows) * ld_mod : nullptr;
     const u16* mh = mscale ? mshift + (size_t)(row / mod_rows) * ld_mod : nullptr;
+    norm_chunks<KIND, WBF16>(v, D, w, b, ms, mh, eps, red);
 #pragma unroll
-    for (int k = 0; k < kMaxChunks; ++k) {
+    for (int k = 0; k < kNormMaxChunks; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
-        if (c < nch) {
-            float o[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int j = 16 * c + i;
-                float t = KIND == 0 ? v[k][i] * r : (v[k][i] - mu) * r;
-                if (w) t = t * ldp<WBF16>(w, j);
-                if (b) t = t + ldp<WBF16>(b, j);
-                if (ms) t = t * (1.f + bf2f(__ldg(ms + j))) + bf2f(__ldg(mh + j));
-                o[i] = t;
-            }
-            store_bf16x16(nout + base + 16 * c, o);
-        }
+        if (c < nch) store_bf16x16(nout + base + 16 * c, v[k]);
     }
 }
 
@@ -147,13 +67,6 @@ __global__ void __launch_bounds__(256) k_rope(const u16* __restrict__ x, u16* __
         orow[h * D + j] = f2bf(p - q);
         orow[h * D + half + j] = f2bf(u + v);
     }
-}
-
-int norm_threads(int D) {
-    int t = ((D >> 4) + 31) & ~31;
-    if (t < 32) t = 32;
-    if (t > 512) t = 512;
-    return t;
 }
 
 template <class Kern, class... Args>
@@ -181,7 +94,7 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
     if (!x || !out || (h && !y) || (!mod_scale != !mod_shift)) return TCQ_ERR_ARG;
     if (kind != 0 && kind != 1) return TCQ_ERR_ARG;
     if (wb_dtype != TCQ_DT_F32 && wb_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
-    if (M <= 0 || D <= 0 || (D & 15) || D > 16 * kMaxChunks * 512) return TCQ_ERR_SHAPE;
+    if (M <= 0 || D <= 0 || (D & 15) || D > 16 * kNormMaxChunks * 512) return TCQ_ERR_SHAPE;
     if (mod_scale && (mod_rows <= 0 || ld_mod < D)) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || !tcq_aligned(out, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)))
         return TCQ_ERR_ALIGN;

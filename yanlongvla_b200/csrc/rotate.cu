@@ -7,9 +7,12 @@
 // registers; the later passes (stride 16, 256, 4096) go through shared memory in an XOR-swizzled layout that keeps
 // every 128-bit store and every 32-float warp access conflict-free. A radix-2^R pass performs exactly the additions
 // of R consecutive radix-2 stages in the same order, so the sums are bit-identical to the reference.
+#include "rownorm.cuh"
 #include "tcq_common.cuh"
 
 namespace {
+
+using namespace tcq;
 
 constexpr int kMaxWidth = 16384;
 
@@ -336,6 +339,78 @@ __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc
     }
 }
 
+// Fused chain of one token row across a residual block boundary: one layer's post, the model's residual add and
+// norm, and the next layer's pre, without the BF16 round trips between them (four launches become one):
+//   y = post(acc)        as k_post: SCALE(acc) -> block Walsh -> * sv -> + bias -> BF16          (acc != NULL)
+//       or y = yg        a BF16 tensor                                                            (yg != NULL)
+//   h = BF16(x + y)      written to hout (h = x when there is no y)
+//   n = norm(h)          norm_chunks with norm_threads(N) threads: the same arithmetic, thread count and sum order as
+//                        tcq_add_norm; BF16(n) written to nout when given
+//   q / q4, scale        = pre(BF16(n), su) as k_pre on a BF16 input                             (su != NULL)
+// Each step is bit-identical to the separate kernel. Shared memory: N floats (Walsh buffer) + N BF16 (y, then n).
+template <int AT, int KIND, bool WBF16>
+__global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+                                               const i8* __restrict__ sv, const float* __restrict__ bias, int lda, int col0,
+                                               const u16* __restrict__ yg, const u16* __restrict__ x, u16* __restrict__ hout,
+                                               u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
+                                               const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
+                                               int ld_mod, float eps, const i8* __restrict__ su, int8_t* __restrict__ q,
+                                               int* __restrict__ q4, float* __restrict__ scale, int ldq, int N) {
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    u16* yb = reinterpret_cast<u16*>(buf + N);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x, nch = N >> 4;
+    const size_t base = (size_t)tok * N;
+    if (acc)                                        // ends with a block barrier: yb complete
+        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rs, sv, bias, N, [&](int i, u16 v) { yb[i] = v; });
+    float v[kNormMaxChunks][16];
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+            load_bf16x16(x + base + 16 * c, v[k]);
+            if (acc || yg) {
+                float t[16];
+                if (acc) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) t[i] = bf2f(yb[16 * c + i]);
+                } else {
+                    load_bf16x16(yg + base + 16 * c, t);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[k][i] = bf16_round(v[k][i] + t[i]);
+                if (hout) store_bf16x16(hout + base + 16 * c, v[k]);
+            }
+        }
+    }
+    const u16* ms = mscale ? mscale + (size_t)(tok / mod_rows) * ld_mod : nullptr;
+    const u16* mh = mscale ? mshift + (size_t)(tok / mod_rows) * ld_mod : nullptr;
+    norm_chunks<KIND, WBF16>(v, N, w, b, ms, mh, eps, red);     // synchronizes: every thread is past its reads of yb
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+            if (nout) store_bf16x16(nout + base + 16 * c, v[k]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) yb[16 * c + i] = f2bf(v[k][i]);
+        }
+    }
+    if (!su) return;
+    __syncthreads();
+    float mx = 0.f;
+    row_walsh(buf, N,
+              [&](int c, float* vv) {
+                  float sg[16];
+                  load_signs16(su + 16 * c, sg);
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) vv[i] = bf2f(yb[16 * c + i]) * sg[i];
+              },
+              [&](int i, float val) { buf[swz(i)] = val; mx = fmaxf(mx, fabsf(val)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
 // Gated-MLP middle (kernels.py:263-278): g = lut(BF16(post(gate))), u = BF16(post(up)), x = BF16(g * u) * su,
 // block Walsh, INT8. Shared memory: N floats + N BF16.
 template <int AT>
@@ -589,6 +664,38 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
         case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
         default: return TCQ_ERR_DTYPE;
     }
+}
+
+int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias, int lda,
+              int col0, const uint16_t* y, const uint16_t* x, uint16_t* h, uint16_t* n, const void* w, const void* b,
+              int wb_dtype, const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps,
+              int kind, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int ldq, int M, int N, void* stream) {
+    if (!x || (acc && y) || (!n && !su) || (!mod_scale != !mod_shift)) return TCQ_ERR_ARG;
+    if (kind != 0 && kind != 1) return TCQ_ERR_ARG;
+    if (wb_dtype != TCQ_DT_F32 && wb_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
+    if (M <= 0 || !width_ok(N)) return TCQ_ERR_SHAPE;
+    if (acc) {
+        if (!sv) return TCQ_ERR_ARG;
+        if (acc_dtype != TCQ_DT_I32 && acc_dtype != TCQ_DT_F32) return TCQ_ERR_DTYPE;
+        if (acc_dtype == TCQ_DT_I32 && (!s || !rs)) return TCQ_ERR_ARG;
+        if (col0 < 0 || lda < col0 + N) return TCQ_ERR_SHAPE;
+        if (!acc_aligned(acc, acc_dtype, lda, col0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
+    }
+    if (su && (!scale || (!q && !q4) || (q4 && ldq < M))) return TCQ_ERR_ARG;
+    if (mod_scale && (mod_rows <= 0 || ld_mod < N)) return TCQ_ERR_ARG;
+    if (!tcq_aligned(x, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)) || (n && !tcq_aligned(n, 16)) ||
+        (su && !tcq_aligned(su, 16)) || (q && !tcq_aligned(q, 16)))
+        return TCQ_ERR_ALIGN;
+    const size_t smem = (size_t)6 * N;
+    const int T = norm_threads(N);
+    const bool wb = wb_dtype == TCQ_DT_BF16, i32 = acc && acc_dtype == TCQ_DT_I32;
+    auto kern = kind == 0 ? (i32 ? (wb ? k_chain<TCQ_DT_I32, 0, true> : k_chain<TCQ_DT_I32, 0, false>)
+                                 : (wb ? k_chain<TCQ_DT_F32, 0, true> : k_chain<TCQ_DT_F32, 0, false>))
+                          : (i32 ? (wb ? k_chain<TCQ_DT_I32, 1, true> : k_chain<TCQ_DT_I32, 1, false>)
+                                 : (wb ? k_chain<TCQ_DT_F32, 1, true> : k_chain<TCQ_DT_F32, 1, false>));
+    return launch(kern, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, lda, col0, (const u16*)y, (const u16*)x,
+                  (u16*)h, (u16*)n, w, b, (const u16*)mod_scale, (const u16*)mod_shift, mod_rows, ld_mod, eps, (const i8*)su, q,
+                  (int*)q4, scale, ldq, N);
 }
 
 static int post_multi(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,

@@ -1,0 +1,119 @@
+// Row norm core shared by tcq_add_norm (norm.cu) and the fused post -> add -> norm -> pre chain (rotate.cu).
+//
+// A thread block owns one row of width D (a multiple of 16); thread t holds the 16-element chunks c = t + k * blockDim
+// (k < kNormMaxChunks) in registers. Row sums run in a fixed order: each thread's elements in index order, a
+// butterfly over the warp (every lane ends with the same sum: floating-point addition is commutative), then the
+// warps' sums in warp order. Both kernels launch norm_threads(D) threads per row, so they reduce identically and
+// their outputs agree bit for bit.
+#pragma once
+#include "tcq_common.cuh"
+
+namespace tcq {
+
+constexpr int kNormMaxChunks = 4;      // rows up to 16 * 4 * 512 = 32768 wide
+
+__host__ __device__ inline int norm_threads(int D) {
+    int t = ((D >> 4) + 31) & ~31;
+    if (t < 32) t = 32;
+    if (t > 512) t = 512;
+    return t;
+}
+
+__device__ __forceinline__ float bf16_round(float f) { return bf2f(f2bf(f)); }
+
+// Sum over the block in a fixed order; every thread receives the same value. `red` holds one float per warp.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();                               // red may still be read by a previous reduction
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+    const int warps = (blockDim.x + 31) >> 5;
+    for (int i = 0; i < warps; ++i) t += red[i];
+    return t;
+}
+
+__device__ __forceinline__ void load_bf16x16(const u16* p, float* v) {
+    const uint4* u = reinterpret_cast<const uint4*>(p);
+    const uint4 a = __ldg(u), b = __ldg(u + 1);
+    const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = bf2f((u16)(w[i] & 0xffffu));
+        v[2 * i + 1] = bf2f((u16)(w[i] >> 16));
+    }
+}
+
+__device__ __forceinline__ void store_bf16x16(u16* p, const float* v) {
+    u32 w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = (u32)f2bf(v[2 * i]) | ((u32)f2bf(v[2 * i + 1]) << 16);
+    uint4* u = reinterpret_cast<uint4*>(p);
+    u[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    u[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// Element j of an FP32 or BF16 parameter vector.
+template <bool WBF16>
+__device__ __forceinline__ float ldp(const void* p, int j) {
+    if (WBF16) return bf2f(__ldg(reinterpret_cast<const u16*>(p) + j));
+    return __ldg(reinterpret_cast<const float*>(p) + j);
+}
+
+// The norm of the row held in v (the residual sum h, already rounded to BF16), in place, unrounded:
+// KIND 0 (RMSNorm):   n = (h * r) * w,                r = rsqrt(sum(h^2) / D + eps)
+// KIND 1 (LayerNorm): n = ((h - mu) * r) * w + b,     mu = sum(h) / D, r = rsqrt(sum((h - mu)^2) / D + eps)
+// w / b optional (NULL = 1 / 0), FP32 or (WBF16) BF16; ms / mh (BF16, NULL = none): n = n * (1 + ms) + mh.
+// Every thread of the block must call it (it synchronizes).
+template <int KIND, bool WBF16>
+__device__ __forceinline__ void norm_chunks(float (&v)[kNormMaxChunks][16], int D, const void* w, const void* b,
+                                            const u16* ms, const u16* mh, float eps, float* red) {
+    const int nch = D >> 4;
+    float part = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) part += KIND == 0 ? v[k][i] * v[k][i] : v[k][i];
+        }
+    }
+    const float tot = block_sum(part, red);
+    float mu = 0.f, r;
+    if (KIND == 0) {
+        r = rsqrtf(tot / (float)D + eps);
+    } else {
+        mu = tot / (float)D;
+        float p2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormMaxChunks; ++k) {
+            const int c = threadIdx.x + k * blockDim.x;
+            if (c < nch) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float d = v[k][i] - mu;
+                    p2 += d * d;
+                }
+            }
+        }
+        r = rsqrtf(block_sum(p2, red) / (float)D + eps);
+    }
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int j = 16 * c + i;
+                float t = KIND == 0 ? v[k][i] * r : (v[k][i] - mu) * r;
+                if (w) t = t * ldp<WBF16>(w, j);
+                if (b) t = t + ldp<WBF16>(b, j);
+                if (ms) t = t * (1.f + bf2f(__ldg(ms + j))) + bf2f(__ldg(mh + j));
+                v[k][i] = t;
+            }
+        }
+    }
+}
+
+}  // namespace tcq

@@ -248,6 +248,52 @@ def add_norm(x, y=None, weight=None, bias=None, eps=1e-6, kind='rms', h_out=None
     return h.view(shape), n.view(shape)
 
 
+def chain(x, kind, weight=None, nbias=None, eps=1e-6, *, acc=None, s=None, rs=None, sv=None, bias=None, col0=0, y=None,
+          mod=None, mod_rows=1, su=None, q=None, q4=None, scale=None, h_out=None, want_n=True):
+    """Fused post -> residual add -> norm -> pre of one block boundary (tcq_chain). x (M, N) BF16 residual; the add
+    takes the post of acc (FP32 z, or INT32 with token scales s and row scales rs; sv / bias of the producing layer,
+    its columns from col0) or a BF16 tensor y; the norm is add_norm's (kind, weight, nbias, eps, mod); with su the next
+    layer's rotation + INT8 quantization goes to q and/or q4 (K/4, ldq) words and scale (M,). Returns (h, n): h the
+    new residual (x itself without an add), n the BF16 norm output (None when want_n is False)."""
+    M, N = x.shape
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise TcqError('chain: x must be contiguous (M, N) BF16')
+    if acc is not None and y is not None:
+        raise TcqError('chain: give acc or y, not both')
+    adt = 0
+    if acc is not None:
+        adt = _dt(acc, (torch.float32, torch.int32), 'chain acc')
+        if acc.dim() != 2 or acc.shape[0] != M or acc.shape[1] < col0 + N:
+            raise TcqError('chain: acc must be (M, >= col0 + N)')
+    if y is not None and (y.shape != x.shape or y.dtype != torch.bfloat16):
+        raise TcqError('chain: y must be (M, N) BF16')
+    wdt = [t.dtype for t in (weight, nbias) if t is not None]
+    if any(d != wdt[0] for d in wdt) or (wdt and wdt[0] not in (torch.float32, torch.bfloat16)):
+        raise TcqError(f'chain: norm weight / bias must both be float32 or both bfloat16, got {wdt}')
+    for t in (weight, nbias, sv, su):
+        if t is not None and t.numel() != N:
+            raise TcqError(f'chain: per-column vectors must have {N} elements')
+    ms = mh = None
+    ld = 0
+    if mod is not None:
+        ms, mh = mod
+        if ms.dtype != torch.bfloat16 or mh.dtype != torch.bfloat16 or ms.shape[-1] != N or ms.stride(-1) != 1 or ms.stride(0) != mh.stride(0):
+            raise TcqError('chain: mod must be BF16 (G, N) views with unit inner stride')
+        ld = ms.stride(0)
+    if su is not None and (scale is None or (q is None and q4 is None)):
+        raise TcqError('chain: the pre needs scale and q and/or q4')
+    h = x if (acc is None and y is None) else (torch.empty_like(x) if h_out is None else h_out)
+    n = torch.empty_like(x) if (want_n or su is None) else None
+    _cuda(x, acc, y, h, n, weight, nbias, sv, bias, su, q, q4, scale)
+    check(lib.tcq_chain(_p(acc), adt, _p(s), _p(rs), _p(sv), _p(bias), 0 if acc is None else acc.shape[1], int(col0),
+                        _p(y), _p(x), None if (acc is None and y is None) else _p(h), _p(n), _p(weight), _p(nbias),
+                        _DT[wdt[0]] if wdt else DT_F32, _p(ms), _p(mh), int(mod_rows), int(ld), float(eps),
+                        {'rms': 0, 'ln': 1}[kind], _p(su), _p(q), _p(q4), _p(scale), 0 if q4 is None else q4.shape[1], M, N,
+                        _stream()), 'tcq_chain')
+    _count('chain')
+    return h, n
+
+
 def rope(x, cos, sin, heads, out=None):
     """Rotary embedding (half-split form) on x (B, T, heads * D) BF16 with cos / sin (T, D/2) FP32 tables."""
     B, T, W = x.shape
