@@ -31,6 +31,7 @@ def test_policy_runtimes_match_reference(built, runtime):
     P, c, layers, obs, a_ref = built
     model, _, info = P.build_policy('cuda', runtime, c, layers=layers)
     assert info['fused_mlps'] == c.llm_layers + c.dit_layers
+    assert info['chains'] == 2 * (c.llm_layers + c.dit_layers)   # every 2-bit block boundary fused
     with torch.no_grad():
         if runtime == 'hybrid':
             modules.decode_chunk(model)
@@ -44,7 +45,12 @@ def test_policy_layers_match_oracle(built):
     """Hook two quantized layers (LLM q/k/v group member, DiT AdaLN at M = batch) and check them against the oracle."""
     from yanlongvla_b200 import modules
     P, c, layers, obs, _ = built
-    model, _, _ = P.build_policy('cuda', 'fly', c, layers=layers)
+    modules.FUSE['chain'] = False                  # the hooks read each layer's input as a tensor
+    try:
+        model, _, info = P.build_policy('cuda', 'fly', c, layers=layers)
+    finally:
+        modules.FUSE['chain'] = True
+    assert info['chains'] == 0
     seen = {}
 
     def hook(name):

@@ -29,9 +29,30 @@ from . import kernels as K
 RUNTIMES = ('reference', 'resident', 'fly', 'hybrid')
 GROUPS = (('q_proj', 'k_proj', 'v_proj'), ('gate_proj', 'up_proj'))
 STATS = dict(group_runs=0, regroup_misses=0, fused_mlps=0)
-FUSE = dict(post3=True, mlp=True, split=True)
+FUSE = dict(post3=True, mlp=True, split=True, chain=True)
 SIMT_MAX_M = 4
 TC_MAX_M = 32
+
+
+class Deferred:
+    """Output of a single-layer group (or fused MLP) whose post has not run yet, for a consumer that fuses it with
+    what follows (the policy's residual add + norm + next pre, kernels.chain). `tensor()` runs the post instead."""
+    def __init__(self, group, acc, b, in_shape):
+        self.group, self.acc, self.b, self.in_shape = group, acc, b, in_shape
+
+    def post_args(self):
+        g, small = self.group, self.acc.dtype == torch.float32
+        return dict(acc=self.acc, s=None if small else self.b['scale'], rs=None if small else g.rs, sv=g.sv, bias=g.bias)
+
+    def tensor(self):
+        return self.group.posts(self.acc, self.b, self.in_shape)[0]
+
+
+class QAct:
+    """A group input already rotated and quantized into the group's buffers (q or q4, scale) by a fused chain: the
+    group skips its own pre. `shape` is the shape of the activation it stands for."""
+    def __init__(self, b, shape):
+        self.b, self.shape = b, shape
 
 
 class Group:
@@ -60,6 +81,7 @@ class Group:
             self.decode()
         self.x = self.outs = None
         self.served = 0
+        self.defer = False          # single-layer groups: return a Deferred instead of running the post
 
     def decode(self, W=None):
         """Dense INT8 weights of the group (rotated basis) into W (Ntot, K)."""
@@ -121,11 +143,17 @@ class Group:
                 K.post(acc, s, None if rs is None else L.rs, L.sv, L.bias, y, col0=c)
         return [y.reshape(*shape[:-1], n) for y, n in zip(ys, self.N)]
 
+    def input(self, x):
+        """Quantized input buffers: a QAct's as they are, a tensor rotated + quantized here."""
+        return x.b if isinstance(x, QAct) else self.quantize(self.prep(x))
+
     def run(self, x):
-        b = self.quantize(self.prep(x))
-        outs = self.posts(self.product(b), b, x.shape)
+        b = self.input(x)
+        acc = self.product(b)
         STATS['group_runs'] += 1
-        return outs
+        if self.defer:
+            return [Deferred(self, acc, b, x.shape)]
+        return self.posts(acc, b, x.shape)
 
     def get(self, x, index):
         if self.x is not x:
@@ -161,11 +189,12 @@ class KGatedMLP(torch.nn.Module):
         super().__init__()
         self.groups = [gate_up, down]
         self.act = act
+        self.defer = False
         self.gate_proj, self.up_proj, self.down_proj = KLinear(gate_up, 0), KLinear(gate_up, 1), KLinear(down, 0)
 
     def forward(self, x):
         gu, down = self.groups
-        b = gu.quantize(gu.prep(x))
+        b = gu.input(x)
         acc = gu.product(b)
         M = acc.shape[0]
         b2 = down.buffers(M, acc.device)
@@ -178,7 +207,8 @@ class KGatedMLP(torch.nn.Module):
         else:
             K.mid2(acc, None if small else b['scale'], None if small else gu.rs, gu.sv, down.su, act=self.act, **b2)
         STATS['fused_mlps'] += 1
-        return down.posts(down.product(b2), b2, x.shape)[0]
+        acc2 = down.product(b2)
+        return Deferred(down, acc2, b2, x.shape) if self.defer else down.posts(acc2, b2, x.shape)[0]
 
 
 class KPlainMLP(torch.nn.Module):
@@ -187,17 +217,19 @@ class KPlainMLP(torch.nn.Module):
         super().__init__()
         self.groups = [fc1, fc2]
         self.act = act
+        self.defer = False
         self.fc1, self.fc2 = KLinear(fc1, 0), KLinear(fc2, 0)
 
     def forward(self, x):
         g1, g2 = self.groups
-        b = g1.quantize(g1.prep(x))
+        b = g1.input(x)
         acc = g1.product(b)
         small = acc.dtype == torch.float32
         b2 = g2.buffers(acc.shape[0], acc.device)
         K.mid1(acc, None if small else b['scale'], None if small else g1.rs, g1.sv, g1.bias, g2.su, act=self.act, **b2)
         STATS['fused_mlps'] += 1
-        return g2.posts(g2.product(b2), b2, x.shape)[0]
+        acc2 = g2.product(b2)
+        return Deferred(g2, acc2, b2, x.shape) if self.defer else g2.posts(acc2, b2, x.shape)[0]
 
 
 # ------------------------------------------------------------------------------------------------ definition runtime

@@ -118,20 +118,44 @@ def rope_tables(T, D, device):
     return ang.cos().contiguous(), ang.sin().contiguous()
 
 
+def _norm(norm, kind, x, delta, weight, bias, eps, mod=None, mod_rows=1):
+    """Residual add + norm of a block boundary. delta: None, a BF16 tensor, or a modules.Deferred (the producing
+    layer's post not yet run). With a consumer group wired to the norm (`norm.consumer`), the next layer's rotation +
+    quantization runs in the same kernel and the normed activation is returned as a modules.QAct for that group.
+    Returns (x + delta, normed activation)."""
+    consumer = getattr(norm, 'consumer', None)
+    if consumer is None and not isinstance(delta, modules.Deferred):
+        return K.add_norm(x, delta, weight, bias, eps, kind, mod=mod, mod_rows=mod_rows)
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    kw = dict(mod=mod, mod_rows=mod_rows)
+    if isinstance(delta, modules.Deferred):
+        kw.update(delta.post_args())
+    elif delta is not None:
+        kw['y'] = delta.reshape(x2.shape)
+    if consumer is None:
+        h, n = K.chain(x2, kind, weight, bias, eps, **kw)
+        return h.view(shape), n.view(shape)
+    b = consumer.buffers(x2.shape[0], x2.device)
+    h, _ = K.chain(x2, kind, weight, bias, eps, su=consumer.su, q=b.get('q'), q4=b.get('q4'), scale=b['scale'],
+                   want_n=False, **kw)
+    return h.view(shape), modules.QAct(b, shape)
+
+
 class RMSNorm(torch.nn.Module):
-    """RMSNorm with FP32 weight, eps 1e-6; `forward(x, delta)` first adds the pending residual delta (one kernel,
-    kernels.add_norm) and returns (x + delta, norm(x + delta))."""
+    """RMSNorm, eps 1e-6; `forward(x, delta)` first adds the pending residual delta (one kernel) and returns
+    (x + delta, norm(x + delta)); see _norm for the fused forms."""
     def __init__(self, d):
         super().__init__()
         self.weight = torch.nn.Parameter(torch.ones(d))
 
     def forward(self, x, delta=None):
-        return K.add_norm(x, delta, self.weight, None, 1e-6, 'rms')
+        return _norm(self, 'rms', x, delta, self.weight, None, 1e-6)
 
 
 class LayerNorm(torch.nn.Module):
-    """LayerNorm (eps 1e-5 as torch's default, FP32 weight / bias when affine) through kernels.add_norm;
-    `forward(x, delta, mod)` as RMSNorm's, with the optional AdaLN modulation (scale, shift) per sample."""
+    """LayerNorm (eps 1e-5 as torch's default, weight / bias when affine); `forward(x, delta, mod)` as RMSNorm's,
+    with the optional AdaLN modulation (scale, shift) per sample."""
     def __init__(self, d, elementwise_affine=True, eps=1e-5):
         super().__init__()
         self.eps = eps
@@ -142,7 +166,7 @@ class LayerNorm(torch.nn.Module):
             self.weight = self.bias = None
 
     def forward(self, x, delta=None, mod=None, mod_rows=1):
-        return K.add_norm(x, delta, self.weight, self.bias, self.eps, 'ln', mod=mod, mod_rows=mod_rows)
+        return _norm(self, 'ln', x, delta, self.weight, self.bias, self.eps, mod, mod_rows)
 
 
 # Blocks take the residual stream x and the pending residual delta of the previous block (None for the first): the
@@ -387,8 +411,42 @@ def build_policy(device='cuda', runtime='fly', c=PolicyConfig(), seed=0, layers=
     for i in range(c.dit_layers):
         mlp_acts[f'dit.{i}.ff'] = 'gelu'
     info = modules.install(model, layers, runtime=runtime, chunk_parts=('dit.',), mlp_acts=mlp_acts)
+    info['chains'] = wire_chains(model) if runtime != 'reference' and modules.FUSE['chain'] else 0
     model.eval()
     return model, layers, info
+
+
+def wire_chains(model):
+    """Fuse every 2-bit block boundary of the LLM and the DiT into one kernel (kernels.chain): the layer before the
+    residual add (o_proj, the MLP's down / fc2) hands its accumulator over unposted, and the norm after it quantizes
+    straight into the next group's buffers (q / k / v, or the MLP's first group). Returns the number of norms wired."""
+    wired = 0
+
+    def consume(norm, target):
+        nonlocal wired
+        group = target.group[0] if isinstance(target, modules.KLinear) else \
+            target.groups[0] if isinstance(target, (modules.KGatedMLP, modules.KPlainMLP)) else None
+        if group is not None:
+            norm.consumer = group
+            wired += 1
+
+    def defer(producer):
+        if isinstance(producer, modules.KLinear) and len(producer.group[0].layers) == 1:
+            producer.group[0].defer = True
+        elif isinstance(producer, (modules.KGatedMLP, modules.KPlainMLP)):
+            producer.defer = True
+
+    for blk in model.llm:
+        consume(blk.input_layernorm, blk.self_attn.q_proj)
+        consume(blk.post_attention_layernorm, blk.mlp)
+        defer(blk.self_attn.o_proj)
+        defer(blk.mlp)
+    for blk in model.dit:
+        consume(blk.norm1, blk.attn1.q_proj)
+        consume(blk.norm3, blk.ff)
+        defer(blk.attn1.o_proj)
+        defer(blk.ff)
+    return wired
 
 
 def synthetic_observations(B, c=PolicyConfig(), device='cuda', seed=0):
