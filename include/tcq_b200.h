@@ -169,6 +169,15 @@ size_t tcq_gemm_tcq_tc_workspace(int M, int N);
 int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z,
                     int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
 
+/* W2 float-activation products (kernels.gemmf_tcq / gemmf_w8, kernels.py:677-696; kernels k_gemmf_*, kernels.py:
+ * 430-489): hT (K, ldh) BF16 rotated activations from tcq_pre_h (token = column), INT8-table weights (the trellis
+ * stream decoded in the kernel with the per-layer tables of t8 and layer bounds nb0 / nb1 in tile rows, or INT8
+ * resident W (N, K)), FP32 accumulation; z (M, N) = (sum_k w h) * rs. Any M (launched in chunks of 16 tokens). The sum
+ * order is fixed (reproducible) but differs from a float64 sum: this path is checked to a tolerance. */
+int tcq_gemmf_tcq(const uint16_t* bits, const int8_t* t8, const uint16_t* hT, const float* rs, float* z, int M, int N, int K,
+                  int ldh, int nb0, int nb1, void* stream);
+int tcq_gemmf_w8(const int8_t* W, const uint16_t* hT, const float* rs, float* z, int M, int N, int K, int ldh, void* stream);
+
 /* Policy glue around the quantized layers (no counterpart in the reference's kernels: its model code runs these as
  * PyTorch ops, e.g. RMSNorm as float/pow/mean/rsqrt/mul/mul/cast). One launch per call, one block per token row.
  *

@@ -204,6 +204,32 @@ def rotate(x, signs, inverse=False, out_dtype=torch.float32, out=None):
     return y.view(*shape)
 
 
+# ------------------------------------------------------------------------------------------------ W2 float path
+def gemmf_tcq(bits, t8, hT, rs, z, K, bounds=(1 << 30, 1 << 30)):
+    """W2 product with the trellis decode fused (reference kernels.gemmf_tcq): hT (K, ld) BF16 rotated activations
+    (pre_h's hT), t8 per-layer INT8 tables, FP32 accumulation -> z (M, N) = (h . w) * rs."""
+    M, N = z.shape
+    _cuda(bits, t8, hT, rs, z)
+    if hT.dtype != torch.bfloat16 or hT.shape[0] != K or hT.shape[1] < M:
+        raise TcqError('gemmf_tcq: hT must be (K, >= M) BF16')
+    check(lib.tcq_gemmf_tcq(_p(bits), _p(t8), _p(hT), _p(rs), _p(z), M, N, K, hT.shape[1], int(bounds[0]), int(bounds[1]),
+                            _stream()), 'tcq_gemmf_tcq')
+    _count('gemmf_tcq')
+    return z
+
+
+def gemmf_w8(W, hT, rs, z):
+    """W2 product on INT8-resident weights W (N, K) (reference kernels.gemmf_w8)."""
+    M, N = z.shape
+    K = W.shape[1]
+    _cuda(W, hT, rs, z)
+    if hT.dtype != torch.bfloat16 or hT.shape[0] != K or hT.shape[1] < M or W.shape[0] != N:
+        raise TcqError('gemmf_w8: hT must be (K, >= M) BF16 and W (N, K)')
+    check(lib.tcq_gemmf_w8(_p(W), _p(hT), _p(rs), _p(z), M, N, K, hT.shape[1], _stream()), 'tcq_gemmf_w8')
+    _count('gemmf_w8')
+    return z
+
+
 # ------------------------------------------------------------------------------------------------ policy glue
 def add_norm(x, y=None, weight=None, bias=None, eps=1e-6, kind='rms', h_out=None, out=None, mod=None, mod_rows=1):
     """Residual add + RMSNorm / LayerNorm in one launch (tcq_add_norm). x, y (..., D) BF16; returns (h, n) with

@@ -32,6 +32,7 @@ STATS = dict(group_runs=0, regroup_misses=0, fused_mlps=0)
 FUSE = dict(post3=True, mlp=True, split=True, chain=True)
 SIMT_MAX_M = 4
 TC_MAX_M = 32
+FLOAT_MAX_M = 16            # W2 float path: fused FP32 products up to this many tokens, BF16 GEMM above
 
 
 class Deferred:
@@ -56,9 +57,10 @@ class QAct:
 
 
 class Group:
-    """One or more layers sharing the input (and its signs): one rotation + quantization, one product."""
-    def __init__(self, layers, mode, act='gelu'):
-        self.layers, self.mode, self.act = layers, mode, act
+    """One or more layers sharing the input (and its signs): one rotation + quantization, one product.
+    a8=False: the W2 float operating point (BF16 activations in the rotated space, FP32 / BF16 products)."""
+    def __init__(self, layers, mode, act='gelu', a8=True):
+        self.layers, self.mode, self.act, self.a8 = layers, mode, act, a8
         self.K = layers[0].n
         for L in layers:
             if L.n != self.K or not torch.equal(L.su, layers[0].su):
@@ -79,6 +81,8 @@ class Group:
         if mode in ('resident', 'chunk'):
             self.W = torch.empty(self.Ntot, self.K, dtype=torch.int8, device=dev)
             self.decode()
+        if not a8:
+            self.tb = [L.t8.to(torch.bfloat16).contiguous() for L in layers]   # BF16 values of the INT8 tables
         self.x = self.outs = None
         self.served = 0
         self.defer = False          # single-layer groups: return a Deferred instead of running the post
@@ -147,7 +151,40 @@ class Group:
         """Quantized input buffers: a QAct's as they are, a tensor rotated + quantized here."""
         return x.b if isinstance(x, QAct) else self.quantize(self.prep(x))
 
+    def run_float(self, x2, shape):
+        """W2 (modules.py:117-145 of the reference): rotated activations rounded to BF16, INT8-table weights. Few
+        tokens: the fused FP32-accumulating products on hT; more: BF16 decode + BF16 tensor-core product (cuBLAS) with
+        FP32 output (the reference rounds this accumulator to BF16; keeping FP32 stays closer to the definition)."""
+        M, dev, outs = x2.shape[0], x2.device, []
+        if M > FLOAT_MAX_M:
+            h = torch.empty(M, self.K, dtype=torch.bfloat16, device=dev)
+            K.pre_h(x2, self.su, h=h)
+            W = torch.empty(self.Ntot, self.K, dtype=torch.bfloat16, device=dev)
+            for L, c, tb in zip(self.layers, self.col0, self.tb):
+                K.decode_bf16(L.bits, tb, W[c:c + L.m])
+            z = torch.mm(h, W.t(), out_dtype=torch.float32) * self.rs[None, :]
+            for L, c in zip(self.layers, self.col0):
+                y = torch.empty(M, L.m, dtype=torch.bfloat16, device=dev)
+                K.post(z, None, None, L.sv, L.bias, y, col0=c)
+                outs.append(y.reshape(*shape[:-1], L.m))
+        else:
+            hT = torch.empty(self.K, M, dtype=torch.bfloat16, device=dev)
+            K.pre_h(x2, self.su, hT=hT)
+            z = torch.empty(M, self.Ntot, dtype=torch.float32, device=dev)
+            if self.W is not None:
+                K.gemmf_w8(self.W, hT, self.rs, z)
+            else:
+                K.gemmf_tcq(self.bits, self.t8, hT, self.rs, z, self.K, self.bounds)
+            for L, c in zip(self.layers, self.col0):
+                y = torch.empty(M, L.m, dtype=torch.bfloat16, device=dev)
+                K.post(z, None, None, L.sv, L.bias, y, col0=c)
+                outs.append(y.reshape(*shape[:-1], L.m))
+        STATS['group_runs'] += 1
+        return outs
+
     def run(self, x):
+        if not self.a8:
+            return self.run_float(self.prep(x), x.shape)
         b = self.input(x)
         acc = self.product(b)
         STATS['group_runs'] += 1
@@ -269,9 +306,11 @@ def _widths(width):
 
 class RefLinear(torch.nn.Module):
     """W2A8 by definition in PyTorch ops on the device (modules.py:209-219): the 'reference' runtime, used only to
-    compare against; the kernel runtimes never call it. Weights decoded once by the decode kernel."""
-    def __init__(self, layer):
+    compare against; the kernel runtimes never call it. Weights decoded once by the decode kernel. a8=False: the same
+    INT8-table weights with FP32 activations (tcq_format.py:137-138), product in float64."""
+    def __init__(self, layer, a8=True):
         super().__init__()
+        self.a8 = a8
         self.layer = [layer]
         self.w8 = layer.w8()
         self.in_features, self.out_features, self.layer_name = layer.n, layer.m, layer.name
@@ -281,6 +320,11 @@ class RefLinear(torch.nn.Module):
         L = self.layer[0]
         shape = x.shape
         h = _fwht(x.float().reshape(-1, shape[-1]) * L.su.float())
+        if not self.a8:
+            y = _fwht((h.double() @ self.w8.double().t()).float() * L.rs[None, :]) * L.sv.float()
+            if L.bias is not None:
+                y = y + L.bias
+            return y.to(torch.bfloat16).reshape(*shape[:-1], -1)
         amax = h.abs().amax(dim=1, keepdim=True)
         s = torch.where(amax > 0, amax / torch.full_like(amax, 127.0), torch.ones_like(amax))
         q = torch.clamp(torch.round(h / s), -127, 127).to(torch.int8)
@@ -297,8 +341,9 @@ def set_submodule(model, name, module):
     setattr(model.get_submodule(parent) if parent else model, leaf, module)
 
 
-def install(model, layers, runtime='fly', chunk_parts=('action_head',), mlp_acts=None):
+def install(model, layers, runtime='fly', chunk_parts=('action_head',), mlp_acts=None, a8=True):
     """Swap the nn.Linear modules named in `layers` ({name: tcq_format.Layer}) for kernel modules (modules.py:246-311).
+    a8=False installs the W2 float operating point (BF16 rotated activations; MLP middles stay unfused).
 
     mlp_acts: {mlp module name: 'gelu' | 'silu'} of the MLPs whose middles are fused (gate_proj/up_proj/down_proj or
     fc1/fc2 children); MLPs not listed keep their own forward and call the KLinear members one by one.
@@ -311,9 +356,10 @@ def install(model, layers, runtime='fly', chunk_parts=('action_head',), mlp_acts
         if not hasattr(m, 'in_features') or not hasattr(m, 'out_features'):
             raise TypeError(f'{name} is {type(m).__name__}, not a Linear')
     info = dict(runtime=runtime, layers=len(names))
+    info['a8'] = a8
     if runtime == 'reference':
         for name in names:
-            set_submodule(model, name, RefLinear(layers[name]))
+            set_submodule(model, name, RefLinear(layers[name], a8=a8))
         return info
     groups, done = [], set()
     for name in names:
@@ -329,13 +375,13 @@ def install(model, layers, runtime='fly', chunk_parts=('action_head',), mlp_acts
                     members = cand
         chunk = runtime == 'hybrid' and any(p in name for p in chunk_parts)
         mode = 'resident' if runtime == 'resident' else 'chunk' if chunk else 'fly'
-        group = Group([layers[n] for n in members], mode)
+        group = Group([layers[n] for n in members], mode, a8=a8)
         for i, n in enumerate(members):
             set_submodule(model, n, KLinear(group, i))
             done.add(n)
         groups.append(group)
     fused = 0
-    if FUSE['mlp'] and mlp_acts:
+    if FUSE['mlp'] and mlp_acts and a8:
         by_name = {g.layers[0].name: g for g in groups}
         for mlp, act in mlp_acts.items():
             p = f'{mlp}.' if mlp else ''
