@@ -40,6 +40,22 @@ def test_int_mm_exact(K, M, Kd, N):
     assert np.array_equal(n(acc), ref), f'{int((n(acc) != ref).sum())} mismatches'
 
 
+@pytest.mark.parametrize('M,Kd,N', [(2304, 1024, 2304), (2300, 1040, 2320), (4096, 512, 4608)])
+def test_int_mm_two_sm_tiles(K, M, Kd, N):
+    """Products large enough for the two-SM 256 x 256 tiles, including M, N and K that are not tile multiples, in all
+    three epilogues (INT32, FP32 and BF16 with the scales)."""
+    q, w = _rand(M, Kd, N, 1)
+    ref = O.int_matmul(q, w)
+    assert np.array_equal(n(K.int_mm(t(q), t(w))), ref)
+    r = np.random.default_rng(2)
+    s_tok = (r.random(M).astype(np.float32) + 0.5) * 1e-2
+    s_ch = (r.random(N).astype(np.float32) + 0.5) * 1e-3
+    z = O.scale_acc(ref, s_tok, s_ch)
+    assert np.array_equal(n(K.int8_gemm(t(q), t(w), t(s_tok), t(s_ch), out_dtype=torch.float32)), z)
+    assert np.array_equal(n(K.int8_gemm(t(q), t(w), t(s_tok), t(s_ch))), O.f32_to_bf16(z))
+    assert K.device_error() == 0
+
+
 def test_int_mm_extremes(K):
     """All-(-127) and all-127 operands: the largest magnitudes the int8 path sees (no saturation, exact INT32)."""
     M, Kd, N = 40, 8192, 256

@@ -230,6 +230,205 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
 }
 
 
+// ------------------------------------------------------------------------------------------------ two-SM INT8 GEMM
+// Large products: a cluster of two CTAs on an SM pair computes a 256-channel x 256-token tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256). Each CTA loads only its own 128 weight rows and its own 128 tokens per
+// K stage (32 KB) with plain TMA loads (no multicast) whose bytes complete on the leader CTA's stage barrier; the pair
+// exchanges the token halves inside the MMA, so each SM streams a third less operand data from L2 per MMA than the
+// single-SM 128 x 256 tile. The leader's thread issues the MMAs; its commits arrive on the barriers of both CTAs
+// (tcgen05.commit multicast); each CTA's epilogue reads its own 128 accumulator lanes (channels) x 256 columns
+// (tokens) from its own TMEM and releases the buffer on the leader's barrier with a remote arrive.
+constexpr int kStages2 = 6;
+constexpr int kHalf = 128;                                   // channels / tokens per CTA of the pair
+
+__device__ __forceinline__ u32 cluster_rank() {
+    u32 r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ u32 map_to_rank(u32 addr, u32 rank) {
+    u32 r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(u32 cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on a barrier of the pair (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(u32 dst, const CUtensorMap* map, u32 bar_cluster, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void mma_i8_pair(u32 d_tmem, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+// Commit the pair's outstanding MMAs to the barrier at this offset in both CTAs.
+__device__ __forceinline__ void mma_commit_pair(u32 bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+                 "h"((unsigned short)3)
+                 : "memory");
+}
+
+constexpr u32 idesc_i8_pair() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((u32)(256 >> 3) << 17) | ((u32)(256 >> 4) << 24);
+}
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
+              const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K) {
+    constexpr int A_BYTES = kHalf * BK, B_BYTES = kHalf * BK;
+    constexpr u32 TMEM_COLS = 512;                           // two 256-column accumulators
+    constexpr u32 IDESC = idesc_i8_pair();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kStages2 * A_BYTES;
+    u64* bars = reinterpret_cast<u64*>(sB + kStages2 * B_BYTES);
+    u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * kStages2 + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages2), tfull0 = smem_u32(bars + 2 * kStages2),
+              tempty0 = smem_u32(bars + 2 * kStages2 + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const u32 rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int tiles_n = (N + 255) / 256, tiles_m = (M + 255) / 256, tiles = tiles_n * tiles_m;
+    const int KB = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kStages2; ++st) {
+            mbar_init(full0 + 8 * st, 1);                    // the leader's producer arrives; both CTAs' bytes complete
+            mbar_init(empty0 + 8 * st, 1);                   // the leader's MMA commit (multicast)
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull0 + 8 * a, 1);                    // the leader's MMA commit (multicast)
+            mbar_init(tempty0 + 8 * a, 8);                   // 4 epilogue warps x 2 CTAs (used in the leader)
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {                                         // the same warp of both CTAs allocates the pair's TMEM
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();                                          // barriers of both CTAs initialized, TMEM allocated
+    tc_fence_after();
+    const u32 tmem = *tmem_slot;
+    pdl_launch_dependents();
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmW) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmQ) : "memory");
+            int stage = 0;
+            u32 phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += pairs) {
+                const int tn = tile % tiles_n, tm = tile / tiles_n;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag)) { ok = false; break; }
+                    const u32 fb = map_to_rank(full0 + 8 * stage, 0);
+                    if (leader) mbar_expect_tx(full0 + 8 * stage, 2 * (A_BYTES + B_BYTES));
+                    tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmW, fb, kb * BK, tn * 256 + (int)rank * kHalf);
+                    tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmQ, fb, kb * BK, tm * 256 + (int)rank * kHalf);
+                    if (++stage == kStages2) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int stage = 0, it = 0;
+            u32 phase = 0;
+            bool ok = true;
+            int committed = -1;
+            for (int tile = pair; tile < tiles && ok; tile += pairs, ++it) {
+                const int a = it & 1;
+                const u32 aph = (it >> 1) & 1;
+                if (!mbar_wait(tempty0 + 8 * a, aph ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const u32 d = tmem + a * 256;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const u32 aaddr = smem_u32(sA + stage * A_BYTES), baddr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)
+                        mma_i8_pair(d, sw128_desc(aaddr + 32 * k), sw128_desc(baddr + 32 * k), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    mma_commit_pair(empty0 + 8 * stage);
+                    if (++stage == kStages2) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull0 + 8 * a);
+                committed = it;
+            }
+            if (!ok && committed >= 0) {
+                volatile int never = 0;
+                mbar_wait(tfull0 + 8 * (committed & 1), (committed >> 1) & 1, &never, 100000000ull);
+            }
+        }
+    } else {
+        const int q = warp & 3;                              // TMEM lane quarter this warp may access
+        const u32 tempty_leader = map_to_rank(tempty0, 0);
+        int it = 0;
+        for (int tile = pair; tile < tiles; tile += pairs, ++it) {
+            const int a = it & 1;
+            const u32 aph = (it >> 1) & 1;
+            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
+            tc_fence_after();
+            const int tn = tile % tiles_n, tm = tile / tiles_n;
+            const int ch = tn * 256 + (int)rank * kHalf + 32 * q + lane, m0 = tm * 256;
+            const bool chok = ch < N;
+            const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 256 / 32; ++c) {
+                u32 v[32];
+                tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * 256 + 32 * c), v);
+                const int t0 = m0 + 32 * c;
+                if (chok) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int tok = t0 + j;
+                        if (tok < M) {
+                            const size_t o = (size_t)tok * N + ch;
+                            if (MODE == OUT_I32) {
+                                reinterpret_cast<int*>(out)[o] = (int)v[j];
+                            } else {
+                                const float z = ((float)(int)v[j] * s_tok[tok]) * sc;
+                                if (MODE == OUT_F32) reinterpret_cast<float*>(out)[o] = z;
+                                else reinterpret_cast<u16*>(out)[o] = f2bf(z);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) remote_arrive(tempty_leader + 8 * a);
+        }
+    }
+    tc_fence_before();
+    cluster_sync();                                          // every MMA done, every TMEM read done in both CTAs
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ fused decode-GEMM
 // z (M, N) FP32 = ((float)(q W^T) * s[t]) * rs[n] with W decoded from the trellis stream straight into shared memory:
 // the decoded weights never leave the SM. One CTA = one 128-channel tile (8 tile rows) x one K range; per 128-byte K
@@ -472,7 +671,31 @@ int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, c
     return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K, ks) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
 }
 
-// Token-tile width: 256 while that still gives a quarter of the SMs a tile (wide tiles re-read the weights least);
+template <int MODE>
+int launch_i8_2sm(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
+                  cudaStream_t st) {
+    CUtensorMap tmW, tmQ;
+    if (!make_map(&tmW, W, N, K, kHalf) || !make_map(&tmQ, q, M, K, kHalf)) return TCQ_ERR_ARG;
+    auto kern = k_gemm_i8_2sm<MODE>;
+    const int smem = 1024 + kStages2 * 2 * kHalf * BK + (2 * kStages2 + 4) * 8 + 16;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
+    const int tiles = ((N + 255) / 256) * ((M + 255) / 256);
+    int pairs = sms() / 2;
+    if (pairs > tiles) pairs = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+}
+
+// Above that, token-tile width: 256 while that still gives a quarter of the SMs a tile (wide tiles re-read the weights least);
 // otherwise the widest of 128 / 64 / 32 that fills half the SMs, so small-M products do not run on a handful of SMs.
 // An INT32 product with too few tiles even at 32 is split along K as well (integer atomics into the zeroed output).
 template <int MODE>
@@ -480,6 +703,8 @@ int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, co
              cudaStream_t st) {
     const int ct = (N + BM - 1) / BM, half = sms() / 2, KB = (K + BK - 1) / BK;
     auto tiles = [&](int bn) { return ct * ((M + bn - 1) / bn); };
+    // Large products: the two-SM 256 x 256 tile once every SM pair gets a tile.
+    if (M >= 512 && ((N + 255) / 256) * ((M + 255) / 256) >= half) return launch_i8_2sm<MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
     if (M > 128 && tiles(256) >= sms() / 4) return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
     if (M > 64 && tiles(128) >= half) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
     if (M > 32 && tiles(64) >= half) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
