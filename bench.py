@@ -387,7 +387,18 @@ def run_reference(args, rank, world):
     )
 
 
+def _claim_stdout():
+    """The driver reads exactly one JSON line from stdout. Libraries print to file descriptor 1 on their own (NCCL's
+    version banner at initialization, for one): point descriptor 1 at stderr and keep a private copy of the original
+    stdout for the result line."""
+    sys.stdout.flush()
+    result = os.fdopen(os.dup(1), 'w')
+    os.dup2(2, 1)
+    return result
+
+
 def main():
+    out_file = _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=50)
@@ -406,7 +417,7 @@ def main():
     if args.impl == 'reference':
         out = run_reference(args, rank, world)
         if out is not None:
-            print(json.dumps(out), flush=True)
+            print(json.dumps(out), file=out_file, flush=True)
         return
     import torch
     dist = None
@@ -424,7 +435,7 @@ def main():
             v, dt, nl = cpu_reference(args.ref_layers + 1, os.cpu_count())
             out['cpu_baseline'] = dict(value=round(v, 6), unit='GB/s', cores=os.cpu_count(), kind='port',
                                        sample='%d config-1 layers (decode + exact product + epilogue), %.1f s' % (nl, dt))
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=out_file, flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
