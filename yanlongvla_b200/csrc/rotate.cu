@@ -41,26 +41,53 @@ __device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bo
 // ld16(c, v): the 16 inputs of chunk c (indices 16c .. 16c+15). fin(i, value): called exactly once per index with the
 // finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]).
 // Ends with a __syncthreads() so that values fin stored to buf are visible to the whole block.
+//
+// Stages h = 1..8 run in registers on a thread's 16 contiguous inputs; h = 16..256 across the 32 lanes of a warp,
+// which hold 32 consecutive chunks (lane partner = lane ^ h/16: the lower lane keeps a + b, the upper b' = a - b, the
+// reference's operands in its order); blocks of up to 512 are then done. Wider blocks finish with radix-16 passes
+// through shared memory at stride 512 (and 8192). Threads per row are a multiple of 32, so a warp's chunks are
+// consecutive; blocks are aligned to their width, so a stage never pairs chunks of different blocks.
 template <class Ld16, class Fin>
 __device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
-    const int nch = K >> 4;
-    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+    const int nch = K >> 4, lane = threadIdx.x & 31;
+    for (int c0 = threadIdx.x - lane; c0 < nch; c0 += blockDim.x) {        // warp-uniform
+        const int c = c0 + lane;
         float v[16];
-        ld16(c, v);
-        bfly<4>(v);
-        const int i0 = c << 4;
-        if (block_of(i0, K) == 16) {
-            const float sc = wscale(16);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) fin(i0 + k, v[k] * sc);
+        int w = 0;                                                             // width of this chunk's block
+        if (c < nch) {
+            ld16(c, v);
+            bfly<4>(v);
+            w = block_of(c << 4, K);
         } else {
-            float4* b4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
+        }
+#pragma unroll
+        for (int st = 0; st < 5; ++st) {
+            const int hc = 1 << st;                                            // stage h = 16 hc
+            if (!__any_sync(0xffffffffu, w > 16 * hc)) break;
+            const bool upper = (lane & hc) != 0, act = w > 16 * hc;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
+                if (act) v[k] = upper ? p - v[k] : v[k] + p;
+            }
+        }
+        if (c < nch) {
+            const int i0 = c << 4;
+            if (w <= 512) {
+                const float sc = wscale(w);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) fin(i0 + k, v[k] * sc);
+            } else {
+                float4* b4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
         }
     }
     __syncthreads();
-    for (int S = 16;; S <<= 4) {
+    for (int S = 512;; S <<= 4) {
         bool work = false;
         int off = 0;
         for (int rem = K; rem;) {
