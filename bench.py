@@ -153,8 +153,7 @@ def run_ours(args, rank, world, dist):
 
     def linear_step():
         for i, Ly in enumerate(layers):
-            K.pre(x[i], Ly['su'], q4=q4[i], scale=s[i])
-            K.gemm_tcq(Ly['bits'], Ly['t8'], q4[i], s[i], Ly['rs'], z[i], M_N)
+            K.gemm_tcq_x(Ly['bits'], Ly['t8'], x[i], Ly['su'], Ly['rs'], z[i], M_N)      # pre fused into the GEMV
             K.post(z[i], None, None, Ly['sv'], None, y[i])
 
     stream = torch.cuda.Stream(device=dev)
@@ -235,7 +234,7 @@ def run_ours(args, rank, world, dist):
                            'traffic: DRAM bytes read + written by one launch of this kernel at this shape '
                            '(ncu --set full capture, profiles/gemm_tcq_m1_4096x4096.md)'),
         e2e=dict(value=round(e2e_gbs, 1), unit='GB/s', h2d_bytes_per_step=int(xh.numel() * 2), d2h_bytes_per_step=int(yh.numel() * 2),
-                 ms_per_step=round(e2e_ms, 4), path='kernels.pre -> gemm_tcq -> post per layer (whole quantized Linear)'),
+                 ms_per_step=round(e2e_ms, 4), path='kernels.gemm_tcq_x (pre fused into the decode-GEMV) -> post per layer (whole quantized Linear)'),
         gpu_launches=args.steps * L,
         clocks=clocks,
         single_layer_us=round(step_ms / L * 1e3, 3),

@@ -161,6 +161,13 @@ int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const fl
 /* Workspace of tcq_gemm_tcq_tc in bytes for (M, N); same zero-filled contract as tcq_gemm_tcq_workspace. */
 size_t tcq_gemm_tcq_tc_workspace(int M, int N);
 
+/* kernels.pre + kernels.gemm_tcq in one launch for 1 <= M <= 4 tokens and K <= 8192 (no single counterpart in the
+ * reference, which launches kernels.pre then kernels.gemm_tcq, kernels.py:602-606, 671-673): every CTA rotates and
+ * quantizes x (M, K) BF16 / F16 / F32 with the input signs su itself, as tcq_pre would (same bits), and runs the fused
+ * decode-GEMV on the result; z as tcq_gemm_tcq. Workspace: tcq_gemm_tcq_workspace(M, N) bytes, same contract. */
+int tcq_gemm_tcq_x(const uint16_t* bits, const int8_t* t8, const void* x, int x_dtype, const int8_t* su, const float* rs,
+                   float* z, int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Tensor-core form of kernels.gemm_tcq (kernels.py:671-673) for 1 <= M <= 256 tokens, and the on-the-fly prefill
  * product of the reference (k_decode + torch._int_mm, modules.py:81-86) without the dense INT8 weights: the trellis
  * stream is decoded straight into shared memory and consumed by tcgen05.mma.kind::i8. q (M, K) int8 row-major

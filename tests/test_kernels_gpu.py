@@ -112,6 +112,39 @@ def test_gemm_tcq_shapes(K, M, N, Kd):
         _eq(n(z), zr, f'gemm_tcq {M}x{N}x{Kd}')
 
 
+@pytest.mark.parametrize('M,N,Kd,dt', [(1, 4096, 4096, 'bf16'), (1, 512, 1152, 'f16'), (2, 2048, 8192, 'f32'),
+                                       (3, 1536, 1536, 'bf16'), (4, 6144, 1152, 'bf16'), (1, 8192, 8192, 'bf16'),
+                                       (4, 48, 80, 'f32')])
+def test_gemm_tcq_x_fused_pre(K, M, N, Kd, dt):
+    """pre fused into the decode-GEMV (tcq_gemm_tcq_x): z equals the oracle's pre + product bit for bit."""
+    L = DevLayer(f'gx{N}x{Kd}', N, Kd, False)
+    x = cases.activations(f'gx{N}x{Kd}', M, Kd, dt)
+    q, s = O.pre(x, dt, L.ref.su)
+    zr = O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs)
+    z = torch.empty(M, N, dtype=torch.float32, device='cuda')
+    for _ in range(2):
+        z.zero_()
+        K.gemm_tcq_x(L.bits, L.t8, x_dev(x, dt), L.su, L.rs, z, Kd)
+        _eq(n(z), zr, f'gemm_tcq_x {M}x{N}x{Kd} {dt}')
+
+
+def test_gemm_tcq_x_three_layers_and_limits(K):
+    Ls = [DevLayer(f'gxq{i}', m, 1152, False) for i, m in enumerate((128, 64, 64))]
+    M = 4
+    x = cases.activations('gxqkv', M, 1152, 'bf16')
+    q, s = O.pre(x, 'bf16', Ls[0].ref.su)
+    bits = torch.cat([L.bits for L in Ls]).contiguous()
+    t8 = torch.cat([L.t8.reshape(-1) for L in Ls]).contiguous()
+    rs = torch.cat([L.rs for L in Ls]).contiguous()
+    z = torch.empty(M, 256, dtype=torch.float32, device='cuda')
+    K.gemm_tcq_x(bits, t8, x_dev(x, 'bf16'), Ls[0].su, rs, z, 1152, bounds=(128 // 16, 192 // 16))
+    zr = np.concatenate([O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs) for L in Ls], 1)
+    _eq(n(z), zr, 'gemm_tcq_x qkv')
+    with pytest.raises(K.TcqError):                 # more than 4 tokens: not this entry point
+        K.gemm_tcq_x(Ls[0].bits, Ls[0].t8, torch.zeros(5, 1152, device='cuda').bfloat16(), Ls[0].su, Ls[0].rs,
+                     torch.empty(5, 128, device='cuda'), 1152)
+
+
 def test_gemm_tcq_three_layers(K):
     """q / k / v concatenated along the rows with their own tables (bounds in tile rows)."""
     Ls = [DevLayer(f'qkv{i}', m, 1152, False) for i, m in enumerate((128, 64, 64))]

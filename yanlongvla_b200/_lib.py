@@ -34,6 +34,7 @@ SIGNATURES = {
     'tcq_gemm_w8': [P, P, P, P, P, I, I, I, P],
     'tcq_gemm_tcq_workspace': [I, I],
     'tcq_gemm_tcq': [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P],
+    'tcq_gemm_tcq_x': [P, P, P, I, P, P, P, I, I, I, I, I, P, SZ, P],
     'tcq_gemm_tcq_noalloc': [P, P, P, P, P, P, I, I, I, I, I, P],
     'tcq_gemm_tcq_noalloc_max_elements': [],
     'tcq_gemm_tcq_tc_workspace': [I, I],

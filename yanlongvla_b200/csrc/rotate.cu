@@ -8,6 +8,7 @@
 // every 128-bit store and every 32-float warp access conflict-free. A radix-2^R pass performs exactly the additions
 // of R consecutive radix-2 stages in the same order, so the sums are bit-identical to the reference.
 #include "rownorm.cuh"
+#include "rowwalsh.cuh"
 #include "tcq_common.cuh"
 
 namespace {
@@ -15,212 +16,6 @@ namespace {
 using namespace tcq;
 
 constexpr int kMaxWidth = 16384;
-
-// ---------------------------------------------------------------------------------------------------- row transform
-template <int R, class Fin>
-__device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bool last, Fin& fin) {
-    const int G = w >> R;
-    const float c = wscale(w);
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
-        const int low = g & (S - 1);
-        const int base = off + (((g - low) << R) | low);
-        float v[1 << R];
-#pragma unroll
-        for (int k = 0; k < (1 << R); ++k) v[k] = buf[swz(base + k * S)];
-        bfly<R>(v);
-        if (last) {
-#pragma unroll
-            for (int k = 0; k < (1 << R); ++k) fin(base + k * S, v[k] * c);
-        } else {
-#pragma unroll
-            for (int k = 0; k < (1 << R); ++k) buf[swz(base + k * S)] = v[k];
-        }
-    }
-}
-
-// ld16(c, v): the 16 inputs of chunk c (indices 16c .. 16c+15). fin(i, value): called exactly once per index with the
-// finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]).
-// Ends with a __syncthreads() so that values fin stored to buf are visible to the whole block.
-//
-// Stages h = 1..8 run in registers on a thread's 16 contiguous inputs; h = 16..256 across the 32 lanes of a warp,
-// which hold 32 consecutive chunks (lane partner = lane ^ h/16: the lower lane keeps a + b, the upper b' = a - b, the
-// reference's operands in its order); blocks of up to 512 are then done. Wider blocks finish with radix-16 passes
-// through shared memory at stride 512 (and 8192). Threads per row are a multiple of 32, so a warp's chunks are
-// consecutive; blocks are aligned to their width, so a stage never pairs chunks of different blocks.
-template <class Ld16, class Fin>
-__device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
-    const int nch = K >> 4, lane = threadIdx.x & 31;
-    for (int c0 = threadIdx.x - lane; c0 < nch; c0 += blockDim.x) {        // warp-uniform
-        const int c = c0 + lane;
-        float v[16];
-        int w = 0;                                                             // width of this chunk's block
-        if (c < nch) {
-            ld16(c, v);
-            bfly<4>(v);
-            w = block_of(c << 4, K);
-        } else {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.f;
-        }
-#pragma unroll
-        for (int st = 0; st < 5; ++st) {
-            const int hc = 1 << st;                                            // stage h = 16 hc
-            if (!__any_sync(0xffffffffu, w > 16 * hc)) break;
-            const bool upper = (lane & hc) != 0, act = w > 16 * hc;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
-                if (act) v[k] = upper ? p - v[k] : v[k] + p;
-            }
-        }
-        if (c < nch) {
-            const int i0 = c << 4;
-            if (w <= 512) {
-                const float sc = wscale(w);
-#pragma unroll
-                for (int k = 0; k < 16; ++k) fin(i0 + k, v[k] * sc);
-            } else {
-                float4* b4 = reinterpret_cast<float4*>(buf);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            }
-        }
-    }
-    __syncthreads();
-    for (int S = 512;; S <<= 4) {
-        bool work = false;
-        int off = 0;
-        for (int rem = K; rem;) {
-            const int w = 1 << (31 - __clz(rem));
-            if (w > S) {
-                work = true;
-                const int L = 31 - __clz(w / S);
-                const bool last = L <= 4;
-                switch (last ? L : 4) {
-                    case 4: walsh_pass<4>(buf, off, w, S, last, fin); break;
-                    case 3: walsh_pass<3>(buf, off, w, S, last, fin); break;
-                    case 2: walsh_pass<2>(buf, off, w, S, last, fin); break;
-                    default: walsh_pass<1>(buf, off, w, S, last, fin); break;
-                }
-            }
-            off += w;
-            rem -= w;
-        }
-        __syncthreads();
-        if (!work) break;
-    }
-}
-
-__device__ __forceinline__ float block_max(float mx, float* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    float r = 0.f;
-    const int warps = (blockDim.x + 31) >> 5;
-    for (int i = 0; i < warps; ++i) r = fmaxf(r, red[i]);
-    return r;
-}
-
-// Per-token INT8 quantizer (tcq_format.py:119-122; kernels.py:164-184): s = amax / 127 (IEEE division, 1 when
-// amax = 0), q = clamp(rint(v / s), -127, 127). q (M, K) row-major and/or q4 (K/4, ldq) words, token = column.
-__device__ __forceinline__ int q8(float v, float s) {
-    float r = rintf(v / s);
-    r = fminf(fmaxf(r, -127.f), 127.f);
-    return (int)r;
-}
-
-__device__ __forceinline__ void quantize_store(const float* buf, float mx, float* red, int8_t* q, int* q4, float* scale,
-                                               int tok, int K, int ldq) {
-    mx = block_max(mx, red);
-    const float s = mx > 0.f ? mx / 127.f : 1.f;
-    if (threadIdx.x == 0) scale[tok] = s;
-    const float4* b4 = reinterpret_cast<const float4*>(buf);
-    for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
-        u32 w[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const float4 v = b4[swz(16 * c + 4 * g) >> 2];
-            w[g] = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
-                   ((u32)(q8(v.w, s) & 0xff) << 24);
-        }
-        if (q) *reinterpret_cast<uint4*>(q + (size_t)tok * K + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
-        if (q4) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) q4[(size_t)(4 * c + g) * ldq + tok] = (int)w[g];
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------------------------------- loaders
-// 16 inputs of a row (BF16 / F16 / F32), 16-byte aligned.
-template <int DT>
-__device__ __forceinline__ void load16(const void* p, float* v) {
-    if (DT == TCQ_DT_F32) {
-        const float4* f = reinterpret_cast<const float4*>(p);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 a = __ldg(f + q);
-            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-        }
-    } else {
-        const uint4* u = reinterpret_cast<const uint4*>(p);
-        const uint4 a = __ldg(u), b = __ldg(u + 1);
-        const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            if (DT == TCQ_DT_BF16) {
-                v[2 * k] = __uint_as_float(w[k] << 16);
-                v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-            } else {
-                v[2 * k] = h2f((u16)(w[k] & 0xffff));
-                v[2 * k + 1] = h2f((u16)(w[k] >> 16));
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void load_signs16(const i8* p, float* sg) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-    const u32 w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
-}
-
-__device__ __forceinline__ void load_f16x(const float* p, float* v) {
-    const float4* f = reinterpret_cast<const float4*>(p);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 a = __ldg(f + q);
-        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-    }
-}
-
-// Scaled accumulator inputs z = SCALE(acc): I32 ((float)a * s) * rs, F32 a, BF16 bf2f(a) * rs (kernels.py:545).
-template <int AT>
-__device__ __forceinline__ void load_scaled16(const void* acc, size_t idx, float s, const float* rs, float* v) {
-    if (AT == TCQ_DT_I32) {
-        const int4* a4 = reinterpret_cast<const int4*>(reinterpret_cast<const int*>(acc) + idx);
-        float r[16];
-        load_f16x(rs, r);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int4 a = __ldg(a4 + q);
-            v[4 * q] = ((float)a.x * s) * r[4 * q];
-            v[4 * q + 1] = ((float)a.y * s) * r[4 * q + 1];
-            v[4 * q + 2] = ((float)a.z * s) * r[4 * q + 2];
-            v[4 * q + 3] = ((float)a.w * s) * r[4 * q + 3];
-        }
-    } else if (AT == TCQ_DT_F32) {
-        load_f16x(reinterpret_cast<const float*>(acc) + idx, v);
-    } else {
-        float r[16];
-        load_f16x(rs, r);
-        load16<TCQ_DT_BF16>(reinterpret_cast<const u16*>(acc) + idx, v);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = v[k] * r[k];
-    }
-}
 
 // ---------------------------------------------------------------------------------------------------- kernels
 template <int DT>

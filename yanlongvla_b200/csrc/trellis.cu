@@ -19,6 +19,7 @@
 
 #include <algorithm>
 
+#include "rowwalsh.cuh"
 #include "trellis_common.cuh"
 
 namespace {
@@ -107,6 +108,7 @@ struct Parts {
 
 constexpr int kMaxRows = 24;
 constexpr int kUnitBytes = 32 * 64;    // one warp's unit of one-lane-per-tile work: 32 tiles
+constexpr int kFxMaxSmem = 220 * 1024; // dynamic shared memory of the decode-GEMV with its pre fused (table + staging + row)
     // tile rows one CTA may touch (the launcher bounds the units per CTA accordingly)
 
 // Sum V = RPT x MT accumulators over the lanes that hold the same row group (lanes differing in bits >= log2(LT)) by
@@ -157,11 +159,15 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
     return old;
 }
 
-template <int MT, int LT>
+// FX (M <= 4): the layer's pre runs in the kernel: after the dependency wait every CTA rotates and quantizes the M
+// activation rows x (BF16 / F16 / F32) itself (the same row_walsh and quantize_store as k_pre, so the same bits) into
+// shared memory, and the decode loop reads its activations and token scales from there; the separate pre launch and
+// its global round trip disappear.
+template <int MT, int LT, bool FX>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* __restrict__ q4, const float* __restrict__ s,
            const float* __restrict__ rs, float* __restrict__ z, int M, int N, int K, Parts parts, int* __restrict__ ws_acc,
-           int* __restrict__ ws_cnt, int act_vec) {
+           int* __restrict__ ws_cnt, int act_vec, const void* __restrict__ xin, int xdt, const i8* __restrict__ su) {
     constexpr int RPT = 16 / LT;    // tile rows per lane (LT lanes share a tile)
     constexpr int TPU = 32 / LT;    // tiles per unit
     constexpr int RV = 16 * MT;     // partial sums per tile row
@@ -172,6 +178,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     __shared__ int racc[kMaxRows * RV];
     __shared__ float srs[kMaxRows * 16];           // row scales of this CTA's tile rows
     __shared__ float ss[MT];                       // token scales
+    __shared__ float red[32];                      // FX: the quantizer's block maximum
     pdl_launch_dependents();
     // This CTA's layer (selected without dynamic indexing of the parameter arrays).
     int cb = parts.cta0[0], tb = parts.tr0[0], slot = parts.slot[0], uq = parts.uq[0], ur = parts.ur[0];
@@ -242,7 +249,31 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     fill_table_i8_nt<kThreads>(tab, pairs);
     __syncthreads();
     pdl_wait();                                    // activations / scales come from the previous kernel
-    const float sv = (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
+    const float sv = !FX && (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
+    // FX: the pre of the M rows into shared memory (Walsh buffer, then q4 words (K/4, M) and ss).
+    float* sbuf = reinterpret_cast<float*>(reinterpret_cast<char*>(tab + kTabBytes / 4) + (CO ? (kThreads / 32) * kUnitBytes : 0));
+    int* sq4 = reinterpret_cast<int*>(sbuf + K);
+    if constexpr (FX) {
+        const size_t es = xdt == TCQ_DT_F32 ? 4 : 2;
+        for (int m = 0; m < M; ++m) {
+            const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
+            float mx = 0.f;
+            row_walsh(sbuf, K,
+                      [&](int cc, float* v) {
+                          float sg[16];
+                          if (xdt == TCQ_DT_BF16) load16<TCQ_DT_BF16>(xr + (size_t)16 * cc * es, v);
+                          else if (xdt == TCQ_DT_F16) load16<TCQ_DT_F16>(xr + (size_t)16 * cc * es, v);
+                          else load16<TCQ_DT_F32>(xr + (size_t)16 * cc * es, v);
+                          load_signs16(su + 16 * cc, sg);
+#pragma unroll
+                          for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
+                      },
+                      [&](int i, float v) { sbuf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+            quantize_store(sbuf, mx, red, nullptr, sq4, ss, m, K, M);
+            __syncthreads();                       // sbuf is rewritten by the next row; sq4 / ss complete
+        }
+    }
+    const int* qsrc = FX ? sq4 : q4;
     for (; u < ue; u += nw) {
         const int tc = seg * TPU + tin;
         u32 W[RPT + 1];
@@ -279,16 +310,17 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         // every lane without a branch (their products add nothing).
         if (CO || tc < tiles) {
             int act[4][MT];
-            const int* qa = q4 + (size_t)4 * tc * M;
+            const int* qa = qsrc + (size_t)4 * tc * M;
             if (MT == 1 && act_vec) {
                 int4 v = make_int4(0, 0, 0, 0);
-                if (!CO || tc < tiles) v = __ldg(reinterpret_cast<const int4*>(qa));
+                if (!CO || tc < tiles) v = FX ? *reinterpret_cast<const int4*>(qa) : __ldg(reinterpret_cast<const int4*>(qa));
                 act[0][0] = v.x; act[1][0] = v.y; act[2][0] = v.z; act[3][0] = v.w;
             } else {
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
 #pragma unroll
-                    for (int m = 0; m < MT; ++m) act[e][m] = (m < M && tc < tiles) ? __ldg(qa + e * M + m) : 0;
+                    for (int m = 0; m < MT; ++m)
+                        act[e][m] = (m < M && tc < tiles) ? (FX ? qa[e * M + m] : __ldg(qa + e * M + m)) : 0;
             }
 #pragma unroll
             for (int a = 0; a < RPT; ++a) {
@@ -313,7 +345,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         seg = sn;
     }
     if ((int)threadIdx.x < nrs) srs[threadIdx.x] = rsv;
-    if (threadIdx.x < MT) ss[threadIdx.x] = sv;
+    if (!FX && threadIdx.x < MT) ss[threadIdx.x] = sv;
     __syncthreads();
     for (int r = warp; r < nrows; r += nw) {
         const int rrel = row_first + r, trow = tb + rrel;
@@ -474,7 +506,8 @@ int decode_grid(int m, int n) {
 
 template <int MT, int LT>
 int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
-                    int M, int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
+                    int M, int N, int K, int nb0, int nb1, int* ws, cudaStream_t st, const void* xin = nullptr, int xdt = 0,
+                    const int8_t* su = nullptr) {
     const int TPU = 32 / LT, tiles = K >> 4, S = (tiles + TPU - 1) / TPU, R = N >> 4;
     Parts p{};
     int bounds[4] = {0, nb0 < R ? nb0 : R, nb1 < R ? nb1 : R, R};
@@ -513,8 +546,10 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
     int max_units = 0;
     for (int l = 0; l < nl; ++l) max_units = std::max(max_units, p.uq[l] + (p.ur[l] > 0 ? 1 : 0));
     p.pf_lead = nl == 1 && max_units <= 2 * (kThreads / 32) ? std::max(1, (cta * 5) / 16) : 0;
-    auto kern = k_gemm_tcq<MT, LT>;
-    const int smem = kTabBytes + (LT == 1 ? (kThreads / 32) * kUnitBytes : 0);
+    const bool fx = xin != nullptr;
+    auto kern = fx ? k_gemm_tcq<MT, LT, (MT <= 4)> : k_gemm_tcq<MT, LT, false>;
+    const int smem = kTabBytes + (LT == 1 ? (kThreads / 32) * kUnitBytes : 0) + (fx ? K * 4 + K * MT : 0);
+    if (fx && (MT > 4 || smem > kFxMaxSmem)) return TCQ_ERR_SHAPE;
     if (set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cta);
@@ -528,9 +563,9 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
     cfg.numAttrs = 1;
     int* ws_acc = ws;
     int* ws_cnt = ws + (size_t)M * N;
-    const int act_vec = tcq_aligned(q4, 16) ? 1 : 0;
+    const int act_vec = fx || tcq_aligned(q4, 16) ? 1 : 0;
     if (cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const u16*>(bits), reinterpret_cast<const i8*>(t8), q4, s, rs, z,
-                           M, N, K, p, ws_acc, ws_cnt, act_vec) != cudaSuccess)
+                           M, N, K, p, ws_acc, ws_cnt, act_vec, xin, xdt, reinterpret_cast<const i8*>(su)) != cudaSuccess)
         return TCQ_ERR_LAUNCH;
     return TCQ_OK;
 }
@@ -539,15 +574,18 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
 // many tiles as the machine has threads (4096 x 4096 and up); on smaller layers two or four lanes split a tile's
 // rows so that every warp still gets work. M <= 4: 4 lanes; larger M: one lane per token slot (MT lanes).
 int dispatch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z, int M,
-                      int N, int K, int nb0, int nb1, int* ws, cudaStream_t st) {
+                      int N, int K, int nb0, int nb1, int* ws, cudaStream_t st, const void* xin = nullptr, int xdt = 0,
+                      const int8_t* su = nullptr) {
     const long long tiles = (long long)(N >> 4) * (K >> 4), lanes = (long long)num_sms() * kThreads;
-    if (M == 1 && tiles * 4 >= lanes * 3) return launch_gemm_tcq<1, 1>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M == 1 && tiles * 8 >= lanes * 3) return launch_gemm_tcq<1, 2>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M == 1) return launch_gemm_tcq<1, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M == 2) return launch_gemm_tcq<2, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 4) return launch_gemm_tcq<4, 4>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 8) return launch_gemm_tcq<8, 8>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    return launch_gemm_tcq<16, 16>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+#define TCQ_GEMV(MT, LT) launch_gemm_tcq<MT, LT>(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st, xin, xdt, su)
+    if (M == 1 && tiles * 4 >= lanes * 3) return TCQ_GEMV(1, 1);
+    if (M == 1 && tiles * 8 >= lanes * 3) return TCQ_GEMV(1, 2);
+    if (M == 1) return TCQ_GEMV(1, 4);
+    if (M == 2) return TCQ_GEMV(2, 4);
+    if (M <= 4) return TCQ_GEMV(4, 4);
+    if (M <= 8) return TCQ_GEMV(8, 8);
+    return TCQ_GEMV(16, 16);
+#undef TCQ_GEMV
 }
 
 template <int MT, int RPW>
@@ -634,6 +672,18 @@ int tcq_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, cons
     int* ws = reinterpret_cast<int*>(workspace);
     cudaStream_t st = (cudaStream_t)stream;
     return dispatch_gemm_tcq(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
+}
+
+int tcq_gemm_tcq_x(const uint16_t* bits, const int8_t* t8, const void* x, int x_dtype, const int8_t* su, const float* rs,
+                   float* z, int M, int N, int K, int nb0, int nb1, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bits || !t8 || !x || !su || !rs || !z) return TCQ_ERR_ARG;
+    if (x_dtype != TCQ_DT_BF16 && x_dtype != TCQ_DT_F16 && x_dtype != TCQ_DT_F32) return TCQ_ERR_DTYPE;
+    if (M < 1 || M > 4 || N <= 0 || K <= 0 || (N & 15) || (K & 15) || K > 8192) return TCQ_ERR_SHAPE;
+    if (!tcq_aligned(bits, 16) || !tcq_aligned(t8, 16) || !tcq_aligned(x, 16) || !tcq_aligned(su, 16)) return TCQ_ERR_ALIGN;
+    if (!workspace || workspace_bytes < tcq_gemm_tcq_workspace(M, N)) return TCQ_ERR_WORKSPACE;
+    if (nb0 < 0 || nb1 < 0) return TCQ_ERR_ARG;
+    return dispatch_gemm_tcq(bits, t8, nullptr, nullptr, rs, z, M, N, K, nb0, nb1, reinterpret_cast<int*>(workspace),
+                             (cudaStream_t)stream, x, x_dtype, su);
 }
 
 int tcq_gemm_w8(const int8_t* W, const int32_t* q4, const float* s, const float* rs, float* z, int M, int N, int K,

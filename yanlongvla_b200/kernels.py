@@ -388,6 +388,23 @@ def gemm_tcq(bits, t8, q4, s, rs, z, K, bounds=(1 << 30, 1 << 30)):
     _count('gemm_tcq')
 
 
+GEMV_X_MAX_M, GEMV_X_MAX_K = 4, 8192
+
+
+def gemm_tcq_x(bits, t8, x, su, rs, z, K, bounds=(1 << 30, 1 << 30)):
+    """pre + gemm_tcq in one launch (tcq_gemm_tcq_x) for M <= 4 tokens and K <= 8192: x (M, K) BF16 / F16 / F32
+    activations, su the layer's input signs; z (M, N) FP32 exactly as pre followed by gemm_tcq."""
+    _cuda(bits, t8, x, su, rs, z)
+    M, N = z.shape
+    if x.shape != (M, K):
+        raise TcqError(f'gemm_tcq_x: x must be ({M}, {K})')
+    dt = _dt(x, (torch.bfloat16, torch.float16, torch.float32), 'gemm_tcq_x')
+    ws = workspace(M, N, z.device)
+    check(lib.tcq_gemm_tcq_x(_p(bits), _p(t8), _p(x), dt, _p(su), _p(rs), _p(z), M, N, K, int(bounds[0]), int(bounds[1]),
+                             _p(ws), ws.numel() * 4, _stream()), 'tcq_gemm_tcq_x')
+    _count('gemm_tcq_x')
+
+
 # ------------------------------------------------------------------------------------------------ W8A8 GEMM
 def int_mm(q, W, out=None):
     """acc (M, N) int32 = q (M, K) int8 @ W (N, K) int8 ^T, exact (tcgen05 kind::i8); replaces torch._int_mm(q, W.t())."""

@@ -29,7 +29,7 @@ from . import kernels as K
 RUNTIMES = ('reference', 'resident', 'fly', 'hybrid')
 GROUPS = (('q_proj', 'k_proj', 'v_proj'), ('gate_proj', 'up_proj'))
 STATS = dict(group_runs=0, regroup_misses=0, fused_mlps=0)
-FUSE = dict(post3=True, mlp=True, split=True, chain=True)
+FUSE = dict(post3=True, mlp=True, split=True, chain=True, pre_gemv=True)
 SIMT_MAX_M = 4
 TC_MAX_M = 32
 FLOAT_MAX_M = 16            # W2 float path: fused FP32 products up to this many tokens, BF16 GEMM above
@@ -182,11 +182,23 @@ class Group:
         STATS['group_runs'] += 1
         return outs
 
+    def acc(self, x):
+        """Accumulator of the group's product and its quantized-input buffers. A tensor input of at most
+        kernels.GEMV_X_MAX_M tokens on the 2-bit stream takes the decode-GEMV with the pre fused (one launch)."""
+        if (FUSE['pre_gemv'] and not isinstance(x, QAct) and self.W is None and self.K <= K.GEMV_X_MAX_K):
+            x2 = self.prep(x)
+            M = x2.shape[0]
+            if M <= min(SIMT_MAX_M, K.GEMV_X_MAX_M):
+                z = torch.empty(M, self.Ntot, dtype=torch.float32, device=x2.device)
+                K.gemm_tcq_x(self.bits, self.t8, x2, self.su, self.rs, z, self.K, self.bounds)
+                return z, dict(scale=None)
+        b = self.input(x)
+        return self.product(b), b
+
     def run(self, x):
         if not self.a8:
             return self.run_float(self.prep(x), x.shape)
-        b = self.input(x)
-        acc = self.product(b)
+        acc, b = self.acc(x)
         STATS['group_runs'] += 1
         if self.defer:
             return [Deferred(self, acc, b, x.shape)]
@@ -231,8 +243,7 @@ class KGatedMLP(torch.nn.Module):
 
     def forward(self, x):
         gu, down = self.groups
-        b = gu.input(x)
-        acc = gu.product(b)
+        acc, b = gu.acc(x)
         M = acc.shape[0]
         b2 = down.buffers(M, acc.device)
         small = acc.dtype == torch.float32
@@ -259,8 +270,7 @@ class KPlainMLP(torch.nn.Module):
 
     def forward(self, x):
         g1, g2 = self.groups
-        b = g1.input(x)
-        acc = g1.product(b)
+        acc, b = g1.acc(x)
         small = acc.dtype == torch.float32
         b2 = g2.buffers(acc.shape[0], acc.device)
         K.mid1(acc, None if small else b['scale'], None if small else g1.rs, g1.sv, g1.bias, g2.su, act=self.act, **b2)
