@@ -215,6 +215,11 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
 int tcq_rope(const uint16_t* x, uint16_t* out, const float* cos_t, const float* sin_t, int rows, int T, int heads, int D,
              int ldx, int ldo, void* stream);
 
+/* Self-test of the failure path (no counterpart in the reference): one thread waits, through the same bounded wait the
+ * tcgen05 kernels use, on a barrier that nothing arrives at; after limit_us (1 .. 1e6) microseconds the wait gives up,
+ * raises device error flag 1 and the kernel returns. Nothing faults and the context stays usable. */
+int tcq_selftest_wait_expiry(unsigned limit_us, void* stream);
+
 /* Device error flags raised by bounded waits inside the kernels (1 = a pipeline wait expired and the kernel stopped
  * early). Synchronizes the current device. reset != 0 clears the flags. Returns -1 if the flags cannot be read. */
 int tcq_device_error(int reset);

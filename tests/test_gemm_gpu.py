@@ -149,3 +149,13 @@ def test_int8_gemm_vision_shapes(K, M, Kd, N):
     q, s = O.quantize_tokens(a)
     out = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc))
     assert np.array_equal(n(out), O.int8_gemm_scaled(q, w, s[:, 0], sc))
+
+
+def test_bounded_wait_expires_and_reports(K):
+    """The failure path of the bounded waits, without a fault: a wait on a barrier nothing arrives at gives up after
+    10 ms and raises the device error flag; the flag clears and the context keeps working."""
+    assert K.device_error(reset=True) == 0
+    assert K.selftest_wait_expiry(10000) == 1
+    assert K.device_error() == 0
+    q, w = _rand(64, 256, 128, 5)
+    assert np.array_equal(n(K.int_mm(t(q), t(w))), O.int_matmul(q, w))

@@ -46,6 +46,7 @@ SIGNATURES = {
     'tcq_add_norm': [P, P, P, P, P, P, I, P, P, I, I, F, I, I, I, P],
     'tcq_rope': [P, P, P, P, I, I, I, I, I, I, P],
     'tcq_chain': [P, I, P, P, P, P, I, I, P, P, P, P, P, P, I, P, P, I, I, F, I, P, P, P, P, I, I, I, P],
+    'tcq_selftest_wait_expiry': [ctypes.c_uint, P],
     'tcq_device_error': [I],
 }
 RESTYPES = {'tcq_status_string': ctypes.c_char_p, 'tcq_gemm_tcq_workspace': SZ, 'tcq_gemm_tcq_tc_workspace': SZ, 'tcq_gemm_tcq_noalloc_max_elements': SZ}

@@ -230,6 +230,21 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
 }
 
 
+// ------------------------------------------------------------------------------------------------ self-test
+// One thread waits, through the kernels' bounded wait, on a barrier that nothing ever arrives at: the wait must give up
+// after limit_ns, raise the device error flag and let the kernel return (a failure path tested without a fault).
+__global__ void k_wait_expiry(unsigned long long limit_ns) {
+    __shared__ __align__(8) u64 bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, limit_ns);
+}
+
 // ------------------------------------------------------------------------------------------------ two-SM INT8 GEMM
 // Large products: a cluster of two CTAs on an SM pair computes a 256-channel x 256-token tile with
 // tcgen05.mma.cta_group::2 (M = 256, N = 256). Each CTA loads only its own 128 weight rows and its own 128 tokens per
@@ -794,6 +809,12 @@ int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, con
     if (M <= 64) return launch_tc<64, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
     if (M <= 128) return launch_tc<128, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
     return launch_tc<256, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+}
+
+int tcq_selftest_wait_expiry(unsigned limit_us, void* stream) {
+    if (limit_us == 0 || limit_us > 1000000) return TCQ_ERR_ARG;
+    k_wait_expiry<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned long long)limit_us * 1000ull);
+    return cudaGetLastError() == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
 }
 
 int tcq_device_error(int reset) {

@@ -429,6 +429,14 @@ def int8_gemm(q, W, s_tok, s_ch, out=None, out_dtype=torch.bfloat16):
     return out
 
 
+def selftest_wait_expiry(limit_us=10000):
+    """Run the bounded-wait failure path once (tcq_selftest_wait_expiry): returns the device error flags afterwards
+    (1 expected), then clears them."""
+    check(lib.tcq_selftest_wait_expiry(int(limit_us), _stream()), 'tcq_selftest_wait_expiry')
+    flags = device_error(reset=True)
+    return flags
+
+
 def device_error(reset=True):
     """Error flags raised by the kernels' bounded pipeline waits (0 = none). Synchronizes the device."""
     return int(lib.tcq_device_error(int(bool(reset))))
