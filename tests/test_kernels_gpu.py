@@ -332,3 +332,22 @@ def test_graph_capture(K):
     torch.cuda.synchronize()
     _eq(n(y), ref, 'graph replay')
     golden.check(f'dit/M{M}/y', n(y))
+
+
+def test_quantizer_ties_and_tiny_scales(K):
+    """The per-token quantizer at its edge cases (the division-free path falls back to the IEEE quotient near
+    half-integers): exact halves with s = 1, quotients a rounding away from halves, a denormal scale whose reciprocal
+    overflows, and an all-zero row; against the oracle's true division."""
+    Kd = 256
+    x = np.zeros((5, Kd), dtype=np.float32)
+    x[0, :-1] = np.arange(-127, 128, dtype=np.float32)[:Kd - 1] + 0.5
+    x[0, -1] = 127.0                                           # amax 127: s = 1, every quotient an exact half
+    s1 = np.float32(0.0123)
+    x[1, :-1] = ((np.arange(Kd - 1, dtype=np.float32) - 127.0) + np.float32(0.5)) * s1
+    x[1, -1] = np.float32(127.0) * s1
+    r = np.random.default_rng(3)
+    x[2] = r.standard_normal(Kd).astype(np.float32) * 7
+    x[3] = r.standard_normal(Kd).astype(np.float32) * np.float32(1e-40)   # denormal amax: 1/s overflows
+    qd, sd = K.quantize(t(x))
+    qo, so = O.quantize_tokens(x)
+    assert np.array_equal(n(qd), qo) and np.array_equal(n(sd), so[:, 0])

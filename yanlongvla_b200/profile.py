@@ -58,6 +58,7 @@ def kernel_classes(graph, warm=3):
 # Small, seeded invocations of one kernel each, for a profiler to capture (nothing is timed or checked here):
 #   python -m yanlongvla_b200.profile gemv [--n 4096] [--k 4096] [--tokens 1] [--launches 4]
 #   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--launches 4]
+#   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
 # kernels.int_mm on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
@@ -88,10 +89,27 @@ def _case_gemm(m, k, n, launches):
         K.int_mm(q, w, out=out)
 
 
+def _case_rows(kind, m, k, launches):
+    """kernels.pre (BF16 -> INT8 + scales) or kernels.rotate (BF16 -> FP32) on an (m, k) activation."""
+    from . import kernels as K
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(13)
+    x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+    su = (torch.randint(0, 2, (k,), device=dev, generator=g) * 2 - 1).to(torch.int8)
+    q = torch.empty(m, k, dtype=torch.int8, device=dev)
+    s = torch.empty(m, device=dev)
+    y = torch.empty(m, k, device=dev)
+    for _ in range(launches):
+        if kind == 'pre':
+            K.pre(x, su, q=q, scale=s)
+        else:
+            K.rotate(x, su, out=y)
+
+
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description='one kernel case for a profiler')
-    ap.add_argument('case', choices=['gemv', 'gemm'])
+    ap.add_argument('case', choices=['gemv', 'gemm', 'pre', 'rotate'])
     ap.add_argument('--m', type=int, default=4096)
     ap.add_argument('--n', type=int, default=None)
     ap.add_argument('--k', type=int, default=None)
@@ -100,8 +118,10 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.case == 'gemv':
         _case_gemv(a.n or 4096, a.k or 4096, a.tokens, a.launches)
-    else:
+    elif a.case == 'gemm':
         _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches)
+    else:
+        _case_rows(a.case, a.m, a.k or 4096, a.launches)
     torch.cuda.synchronize()
     from . import kernels as K
     err = K.device_error()
