@@ -14,16 +14,28 @@ using namespace tcq;
 
 // h = x (+ y, rounded to BF16 as a BF16 tensor add does); written to hout when given; out = BF16(norm_chunks(h)).
 // Modulation vectors: row group g = row / mod_rows (rows of one sample), row stride ld_mod.
+// stage: the norm weights are copied into shared memory before the dependency wait (dynamic shared memory holds
+// them); the modulation values of the first chunk are loaded with x and y.
 template <int KIND, bool WBF16>
 __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
                                                  u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
                                                  const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
-                                                 int ld_mod, float eps, int D) {
+                                                 int ld_mod, float eps, int D, int stage) {
+    extern __shared__ __align__(16) char cst[];
     __shared__ float red[32];
     pdl_launch_dependents();
+    char* sp = cst;
+    const void* ws = stage_const(sp, w, (WBF16 ? 2 : 4) * D, stage != 0);
+    const void* bs = stage_const(sp, b, (WBF16 ? 2 : 4) * D, stage != 0);
+    __syncthreads();
     pdl_wait();
     const int row = blockIdx.x, nch = D >> 4;
     const size_t base = (size_t)row * D;
+    const u16* ms = mscale ? mscale + (size_t)(row / mod_rows) * ld_mod : nullptr;
+    const u16* mh = mscale ? mshift + (size_t)(row / mod_rows) * ld_mod : nullptr;
+    ModChunk m0{};
+    if (ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0 && (int)threadIdx.x < nch)
+        load_mod_chunk(m0, ms + 16 * threadIdx.x, mh + 16 * threadIdx.x);
     float v[kNormMaxChunks][16];
 #pragma unroll
     for (int k = 0; k < kNormMaxChunks; ++k) {
@@ -39,9 +51,7 @@ __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, cons
             }
         }
     }
-    const u16* ms = mscale ? mscale + (size_t)(row / mod_rows) * ld_mod : nullptr;
-    const u16* mh = mscale ? mshift + (size_t)(row / mod_rows) * ld_mod : nullptr;
-    norm_chunks<KIND, WBF16>(v, D, w, b, ms, mh, eps, red);
+    norm_chunks<KIND, WBF16>(v, D, ws, bs, ms, mh, eps, red, m0);
 #pragma unroll
     for (int k = 0; k < kNormMaxChunks; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
@@ -70,11 +80,13 @@ __global__ void __launch_bounds__(256) k_rope(const u16* __restrict__ x, u16* __
 }
 
 template <class Kern, class... Args>
-int launch_rows(Kern kern, int rows, int threads, void* stream, Args... args) {
+int launch_rows(Kern kern, int rows, int threads, int smem, void* stream, Args... args) {
+    if (smem > 46 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rows);
     cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -101,15 +113,17 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
     const int T = norm_threads(D);
     const bool wb = wb_dtype == TCQ_DT_BF16;
     auto kern = kind == 0 ? (wb ? k_addnorm<0, true> : k_addnorm<0, false>) : (wb ? k_addnorm<1, true> : k_addnorm<1, false>);
-    return launch_rows(kern, M, T, stream, (const u16*)x, (const u16*)y, (u16*)h, (u16*)out, w, b, (const u16*)mod_scale,
-                       (const u16*)mod_shift, mod_rows, ld_mod, eps, D);
+    const int cbytes = ((w ? 1 : 0) + (b ? 1 : 0)) * (wb ? 2 : 4) * D;
+    const int stage = cbytes > 0 && tcq_stage_rows(M, cbytes, kStageMaxBytes);
+    return launch_rows(kern, M, T, stage ? cbytes : 0, stream, (const u16*)x, (const u16*)y, (u16*)h, (u16*)out, w, b,
+                       (const u16*)mod_scale, (const u16*)mod_shift, mod_rows, ld_mod, eps, D, stage);
 }
 
 int tcq_rope(const uint16_t* x, uint16_t* out, const float* cos_t, const float* sin_t, int rows, int T, int heads, int D,
              int ldx, int ldo, void* stream) {
     if (!x || !out || !cos_t || !sin_t) return TCQ_ERR_ARG;
     if (rows <= 0 || T <= 0 || heads <= 0 || D <= 0 || (D & 1) || ldx < heads * D || ldo < heads * D) return TCQ_ERR_SHAPE;
-    return launch_rows(k_rope, rows, 256, stream, (const u16*)x, (u16*)out, cos_t, sin_t, T, heads, D, ldx, ldo);
+    return launch_rows(k_rope, rows, 256, 0, stream, (const u16*)x, (u16*)out, cos_t, sin_t, T, heads, D, ldx, ldo);
 }
 
 }  // extern "C"

@@ -129,13 +129,18 @@ __device__ __forceinline__ void post_row(float* buf, const void* acc, size_t bas
 template <int AT>
 __global__ void __launch_bounds__(512) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, u16* __restrict__ y, int M,
-                                              int N, int lda, int col0) {
+                                              int N, int lda, int col0, int stage) {
     extern __shared__ __align__(16) float buf[];
     pdl_launch_dependents();
+    char* sp = reinterpret_cast<char*>(buf + N);    // layer constants (tcq_post sizes the same set)
+    const float* rsc = static_cast<const float*>(stage_const(sp, AT != TCQ_DT_F32 ? rs : nullptr, 4 * N, stage != 0));
+    const float* biasc = static_cast<const float*>(stage_const(sp, bias, 4 * N, stage != 0));
+    const i8* svc = static_cast<const i8*>(stage_const(sp, sv, N, stage != 0));
+    __syncthreads();
     pdl_wait();
     const int tok = blockIdx.x;
     u16* yo = y + (size_t)tok * N;
-    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rs, sv, bias, N, [&](int i, u16 b) { yo[i] = b; });
+    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 b) { yo[i] = b; });
 }
 
 // Several layers sharing the accumulator row. grid.y == 1: the layers one after another in one block (post3);
@@ -144,20 +149,30 @@ template <int AT>
 __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc, const float* __restrict__ s,
                                                     const float* __restrict__ rs, const i8* __restrict__ sv,
                                                     const float* __restrict__ bias, const u16* __restrict__ lut, u16* y0, u16* y1,
-                                                    u16* y2, int M, int n0, int n1, int n2, int lda, int act0) {
+                                                    u16* y2, int M, int n0, int n1, int n2, int lda, int act0, int nmax,
+                                                    int stage) {
     extern __shared__ __align__(16) float buf[];
     pdl_launch_dependents();
+    const int seg_begin = gridDim.y == 1 ? 0 : blockIdx.y, seg_end = gridDim.y == 1 ? 3 : blockIdx.y + 1;
+    // The constants of this block's columns [cs, ce) into shared memory (after the nmax-float Walsh buffer).
+    const int cs = seg_begin == 0 ? 0 : seg_begin == 1 ? n0 : n0 + n1;
+    const int ce = seg_end == 1 ? n0 : seg_end == 2 ? n0 + n1 : n0 + n1 + n2;
+    char* sp = reinterpret_cast<char*>(buf + nmax);
+    const bool on = stage != 0;
+    const float* rsc = static_cast<const float*>(stage_const(sp, AT != TCQ_DT_F32 && rs ? rs + cs : nullptr, 4 * (ce - cs), on));
+    const float* biasc = static_cast<const float*>(stage_const(sp, bias ? bias + cs : nullptr, 4 * (ce - cs), on));
+    const i8* svc = static_cast<const i8*>(stage_const(sp, sv + cs, ce - cs, on));
+    __syncthreads();
     pdl_wait();
     const int tok = blockIdx.x;
-    const int seg_begin = gridDim.y == 1 ? 0 : blockIdx.y, seg_end = gridDim.y == 1 ? 3 : blockIdx.y + 1;
     for (int seg = seg_begin; seg < seg_end; ++seg) {
         const int N = seg == 0 ? n0 : seg == 1 ? n1 : n2;
         if (N == 0) continue;
         const int c0 = seg == 0 ? 0 : seg == 1 ? n0 : n0 + n1;
         u16* yo = (seg == 0 ? y0 : seg == 1 ? y1 : y2) + (size_t)tok * N;
         const bool act = act0 && seg == 0;
-        post_row<AT>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rs ? rs + c0 : nullptr, sv + c0,
-                     bias ? bias + c0 : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; });
+        post_row<AT>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rsc ? rsc + (c0 - cs) : nullptr, svc + (c0 - cs),
+                     biasc ? biasc + (c0 - cs) : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; });
     }
 }
 
@@ -177,27 +192,58 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
                                                u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
                                                const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
                                                int ld_mod, float eps, const i8* __restrict__ su, int8_t* __restrict__ q,
-                                               int* __restrict__ q4, float* __restrict__ scale, int ldq, int N) {
+                                               int* __restrict__ q4, float* __restrict__ scale, int ldq, int N, int stage) {
     extern __shared__ __align__(16) float buf[];
     __shared__ float red[32];
     u16* yb = reinterpret_cast<u16*>(buf + N);
     pdl_launch_dependents();
+    // Layer constants into shared memory while the previous kernel drains (tcq_chain sizes the same set).
+    char* sp = reinterpret_cast<char*>(yb + N);
+    const bool on = stage != 0;
+    const float* rsc = static_cast<const float*>(stage_const(sp, acc && AT != TCQ_DT_F32 ? rs : nullptr, 4 * N, on));
+    const float* biasc = static_cast<const float*>(stage_const(sp, acc ? bias : nullptr, 4 * N, on));
+    const i8* svc = static_cast<const i8*>(stage_const(sp, acc ? sv : nullptr, N, on));
+    const void* wc = stage_const(sp, w, (WBF16 ? 2 : 4) * N, on);
+    const void* bc = stage_const(sp, b, (WBF16 ? 2 : 4) * N, on);
+    const i8* suc = static_cast<const i8*>(stage_const(sp, su, N, on));
+    __syncthreads();
     pdl_wait();
     const int tok = blockIdx.x, nch = N >> 4;
     const size_t base = (size_t)tok * N;
+    // The thread's first chunk of x (and of y / the modulation) is requested now, with the accumulators, so that the
+    // residual add and the norm do not wait on another global round trip.
+    const bool first = (int)threadIdx.x < nch;
+    const u16* ms = mscale ? mscale + (size_t)(tok / mod_rows) * ld_mod : nullptr;
+    const u16* mh = mscale ? mshift + (size_t)(tok / mod_rows) * ld_mod : nullptr;
+    uint4 x0a = make_uint4(0, 0, 0, 0), x0b = x0a, y0a = x0a, y0b = x0a;
+    ModChunk m0{};
+    if (first) {
+        const uint4* xp = reinterpret_cast<const uint4*>(x + base + 16 * threadIdx.x);
+        x0a = __ldg(xp);
+        x0b = __ldg(xp + 1);
+        if (!acc && yg) {
+            const uint4* yp = reinterpret_cast<const uint4*>(yg + base + 16 * threadIdx.x);
+            y0a = __ldg(yp);
+            y0b = __ldg(yp + 1);
+        }
+        if (ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0) load_mod_chunk(m0, ms + 16 * threadIdx.x, mh + 16 * threadIdx.x);
+    }
     if (acc)                                        // ends with a block barrier: yb complete
-        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rs, sv, bias, N, [&](int i, u16 v) { yb[i] = v; });
+        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 v) { yb[i] = v; });
     float v[kNormMaxChunks][16];
 #pragma unroll
     for (int k = 0; k < kNormMaxChunks; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
-            load_bf16x16(x + base + 16 * c, v[k]);
+            if (k == 0) unpack_bf16x16(x0a, x0b, v[k]);
+            else load_bf16x16(x + base + 16 * c, v[k]);
             if (acc || yg) {
                 float t[16];
                 if (acc) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) t[i] = bf2f(yb[16 * c + i]);
+                } else if (k == 0) {
+                    unpack_bf16x16(y0a, y0b, t);
                 } else {
                     load_bf16x16(yg + base + 16 * c, t);
                 }
@@ -207,9 +253,7 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
             }
         }
     }
-    const u16* ms = mscale ? mscale + (size_t)(tok / mod_rows) * ld_mod : nullptr;
-    const u16* mh = mscale ? mshift + (size_t)(tok / mod_rows) * ld_mod : nullptr;
-    norm_chunks<KIND, WBF16>(v, N, w, b, ms, mh, eps, red);     // synchronizes: every thread is past its reads of yb
+    norm_chunks<KIND, WBF16>(v, N, wc, bc, ms, mh, eps, red, m0);   // synchronizes: every thread is past its reads of yb
 #pragma unroll
     for (int k = 0; k < kNormMaxChunks; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
@@ -225,7 +269,7 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
     row_walsh(buf, N,
               [&](int c, float* vv) {
                   float sg[16];
-                  load_signs16(su + 16 * c, sg);
+                  load_signs16_any(suc + 16 * c, sg);
 #pragma unroll
                   for (int i = 0; i < 16; ++i) vv[i] = bf2f(yb[16 * c + i]) * sg[i];
               },
@@ -239,21 +283,27 @@ template <int AT>
 __global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const u16* __restrict__ lut, const i8* __restrict__ su,
                                               int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M, int N,
-                                              int lda, int ldq) {
+                                              int lda, int ldq, int stage) {
     extern __shared__ __align__(16) float buf[];
     __shared__ float red[32];
     u16* gb = reinterpret_cast<u16*>(buf + N);
     pdl_launch_dependents();
+    char* sp = reinterpret_cast<char*>(gb + N);     // layer constants of the gate and up layers and the next pre
+    const bool on = stage != 0;
+    const float* rsc = static_cast<const float*>(stage_const(sp, AT != TCQ_DT_F32 ? rs : nullptr, 8 * N, on));
+    const i8* svc = static_cast<const i8*>(stage_const(sp, sv, 2 * N, on));
+    const i8* suc = static_cast<const i8*>(stage_const(sp, su, N, on));
+    __syncthreads();
     pdl_wait();
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * lda;
     const float st = s ? s[tok] : 1.f;
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rs ? rs + 16 * c : nullptr, v); },
-              [&](int i, float v) { gb[i] = lut[f2bf(v * (float)sv[i])]; });
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + N + 16 * c, st, rs ? rs + N + 16 * c : nullptr, v); },
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
+              [&](int i, float v) { gb[i] = lut[f2bf(v * (float)svc[i])]; });
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + N + 16 * c, st, rsc ? rsc + N + 16 * c : nullptr, v); },
               [&](int i, float v) {
-                  const u16 u = f2bf(v * (float)sv[N + i]);
-                  buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)su[i];
+                  const u16 u = f2bf(v * (float)svc[N + i]);
+                  buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)suc[i];
               });
     float mx = 0.f;
     row_walsh(buf, N,
@@ -274,19 +324,26 @@ template <int AT>
 __global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, const u16* __restrict__ lut,
                                               const i8* __restrict__ su, int8_t* __restrict__ q, int* __restrict__ q4,
-                                              float* __restrict__ scale, int M, int N, int lda, int ldq) {
+                                              float* __restrict__ scale, int M, int N, int lda, int ldq, int stage) {
     extern __shared__ __align__(16) float buf[];
     __shared__ float red[32];
     pdl_launch_dependents();
+    char* sp = reinterpret_cast<char*>(buf + N);    // layer constants
+    const bool on = stage != 0;
+    const float* rsc = static_cast<const float*>(stage_const(sp, AT != TCQ_DT_F32 ? rs : nullptr, 4 * N, on));
+    const float* biasc = static_cast<const float*>(stage_const(sp, bias, 4 * N, on));
+    const i8* svc = static_cast<const i8*>(stage_const(sp, sv, N, on));
+    const i8* suc = static_cast<const i8*>(stage_const(sp, su, N, on));
+    __syncthreads();
     pdl_wait();
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * lda;
     const float st = s ? s[tok] : 1.f;
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rs ? rs + 16 * c : nullptr, v); },
+    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
               [&](int i, float v) {
-                  v = v * (float)sv[i];
-                  if (bias) v = v + bias[i];
-                  buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)su[i];
+                  v = v * (float)svc[i];
+                  if (biasc) v = v + biasc[i];
+                  buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)suc[i];
               });
     float mx = 0.f;
     row_walsh(buf, N,
@@ -478,12 +535,15 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
     if (M <= 0 || !width_ok(N) || col0 < 0 || lda < col0 + N) return TCQ_ERR_SHAPE;
     if (!acc_aligned(acc, acc_dtype, lda, col0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
-    const size_t smem = (size_t)4 * N;
+    // Staged layer constants (as k_post stages them): rs (I32 / BF16 accumulators), bias, sv.
+    const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N;
+    const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
+    const size_t smem = (size_t)4 * N + (st ? cb : 0);
     const int T = threads_for(N);
     switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
-        case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
-        case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0);
+        case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
+        case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
+        case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
         default: return TCQ_ERR_DTYPE;
     }
 }
@@ -508,16 +568,20 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
     if (!tcq_aligned(x, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)) || (n && !tcq_aligned(n, 16)) ||
         (su && !tcq_aligned(su, 16)) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
-    const size_t smem = (size_t)6 * N;
     const int T = norm_threads(N);
     const bool wb = wb_dtype == TCQ_DT_BF16, i32 = acc && acc_dtype == TCQ_DT_I32;
+    // Layer constants staged by the kernel (the same set, in bytes): rs (I32 accumulators), bias, sv, w, b, su.
+    const size_t cb = (acc ? (size_t)(i32 ? 4 * N : 0) + (bias ? 4 * N : 0) + N : 0) + (size_t)(w ? 1 : 0) * (wb ? 2 : 4) * N +
+                      (size_t)(b ? 1 : 0) * (wb ? 2 : 4) * N + (su ? N : 0);
+    const int stage = tcq_stage_rows(M, cb, kStageMaxBytes);
+    const size_t smem = (size_t)6 * N + (stage ? cb : 0);
     auto kern = kind == 0 ? (i32 ? (wb ? k_chain<TCQ_DT_I32, 0, true> : k_chain<TCQ_DT_I32, 0, false>)
                                  : (wb ? k_chain<TCQ_DT_F32, 0, true> : k_chain<TCQ_DT_F32, 0, false>))
                           : (i32 ? (wb ? k_chain<TCQ_DT_I32, 1, true> : k_chain<TCQ_DT_I32, 1, false>)
                                  : (wb ? k_chain<TCQ_DT_F32, 1, true> : k_chain<TCQ_DT_F32, 1, false>));
     return launch(kern, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, lda, col0, (const u16*)y, (const u16*)x,
                   (u16*)h, (u16*)n, w, b, (const u16*)mod_scale, (const u16*)mod_shift, mod_rows, ld_mod, eps, (const i8*)su, q,
-                  (int*)q4, scale, ldq, N);
+                  (int*)q4, scale, ldq, N, stage);
 }
 
 static int post_multi(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
@@ -535,12 +599,16 @@ static int post_multi(const void* acc, int acc_dtype, const float* s, const floa
     const int nmax = n0 > n1 ? (n0 > n2 ? n0 : n2) : (n1 > n2 ? n1 : n2);
     const int layers = 1 + (n1 > 0) + (n2 > 0);
     const dim3 grid(M, per_layer_blocks ? layers : 1);
-    const size_t smem = (size_t)4 * nmax;
+    // Staged layer constants of a block's columns (at most all n0 + n1 + n2 of them): rs, bias, sv.
+    const size_t ntot = (size_t)n0 + n1 + n2;
+    const size_t cb = ntot * ((acc_dtype != TCQ_DT_F32 && rs ? 4 : 0) + (bias ? 4 : 0) + 1);
+    const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
+    const size_t smem = (size_t)4 * nmax + (st ? cb : 0);
     const int T = threads_for(nmax);
     switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
-        case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
-        case TCQ_DT_BF16: return launch(k_post_multi<TCQ_DT_BF16>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0);
+        case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
+        case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
+        case TCQ_DT_BF16: return launch(k_post_multi<TCQ_DT_BF16>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
         default: return TCQ_ERR_DTYPE;
     }
 }
@@ -565,12 +633,15 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!acc_aligned(acc, acc_dtype, lda, N) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
-    const size_t smem = (size_t)6 * N;
+    // Staged layer constants (as k_mid2 stages them): rs of both layers (I32 / BF16 accumulators), sv of both, su.
+    const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 8 * N : 0) + 2 * N + N;
+    const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
+    const size_t smem = (size_t)6 * N + (st ? cb : 0);
     const int T = threads_for(N);
     switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
-        case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
-        case TCQ_DT_BF16: return launch(k_mid2<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+        case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+        case TCQ_DT_BF16: return launch(k_mid2<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
         default: return TCQ_ERR_DTYPE;
     }
 }
@@ -585,12 +656,15 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!acc_aligned(acc, acc_dtype, lda, 0) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
-    const size_t smem = (size_t)4 * N;
+    // Staged layer constants (as k_mid1 stages them): rs (I32 / BF16 accumulators), bias, sv, su.
+    const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N + N;
+    const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
+    const size_t smem = (size_t)4 * N + (st ? cb : 0);
     const int T = threads_for(N);
     switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
-        case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
-        case TCQ_DT_BF16: return launch(k_mid1<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq);
+        case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+        case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+        case TCQ_DT_BF16: return launch(k_mid1<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
         default: return TCQ_ERR_DTYPE;
     }
 }

@@ -11,6 +11,7 @@
 namespace tcq {
 
 constexpr int kNormMaxChunks = 4;      // rows up to 16 * 4 * 512 = 32768 wide
+constexpr int kStageMaxBytes = 64 * 1024;   // layer constants staged in shared memory per block (stage_const), at most
 
 __host__ __device__ inline int norm_threads(int D) {
     int t = ((D >> 4) + 31) & ~31;
@@ -34,15 +35,18 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return t;
 }
 
-__device__ __forceinline__ void load_bf16x16(const u16* p, float* v) {
-    const uint4* u = reinterpret_cast<const uint4*>(p);
-    const uint4 a = __ldg(u), b = __ldg(u + 1);
+__device__ __forceinline__ void unpack_bf16x16(const uint4& a, const uint4& b, float* v) {
     const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         v[2 * i] = bf2f((u16)(w[i] & 0xffffu));
         v[2 * i + 1] = bf2f((u16)(w[i] >> 16));
     }
+}
+
+__device__ __forceinline__ void load_bf16x16(const u16* p, float* v) {
+    const uint4* u = reinterpret_cast<const uint4*>(p);
+    unpack_bf16x16(__ldg(u), __ldg(u + 1), v);
 }
 
 __device__ __forceinline__ void store_bf16x16(u16* p, const float* v) {
@@ -54,21 +58,40 @@ __device__ __forceinline__ void store_bf16x16(u16* p, const float* v) {
     u[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-// Element j of an FP32 or BF16 parameter vector.
+// Element j of an FP32 or BF16 parameter vector, in global memory or a shared-memory copy (stage_const).
 template <bool WBF16>
 __device__ __forceinline__ float ldp(const void* p, int j) {
-    if (WBF16) return bf2f(__ldg(reinterpret_cast<const u16*>(p) + j));
-    return __ldg(reinterpret_cast<const float*>(p) + j);
+    if (WBF16) return bf2f(reinterpret_cast<const u16*>(p)[j]);
+    return reinterpret_cast<const float*>(p)[j];
 }
+
+// Modulation values of a thread's first chunk, loaded early (with the row's other inputs) into registers: BF16
+// pairs, element i of the chunk in the low (even i) or high (odd i) half of word i / 2.
+struct ModChunk {
+    u32 s[8], h[8];
+    bool on;
+};
+
+__device__ __forceinline__ void load_mod_chunk(ModChunk& m, const u16* ms, const u16* mh) {
+    const uint4* a = reinterpret_cast<const uint4*>(ms);
+    const uint4* b = reinterpret_cast<const uint4*>(mh);
+    const uint4 a0 = __ldg(a), a1 = __ldg(a + 1), b0 = __ldg(b), b1 = __ldg(b + 1);
+    m.s[0] = a0.x; m.s[1] = a0.y; m.s[2] = a0.z; m.s[3] = a0.w; m.s[4] = a1.x; m.s[5] = a1.y; m.s[6] = a1.z; m.s[7] = a1.w;
+    m.h[0] = b0.x; m.h[1] = b0.y; m.h[2] = b0.z; m.h[3] = b0.w; m.h[4] = b1.x; m.h[5] = b1.y; m.h[6] = b1.z; m.h[7] = b1.w;
+    m.on = true;
+}
+
+__device__ __forceinline__ float bf_half(u32 w, int i) { return __uint_as_float((i & 1) ? (w & 0xffff0000u) : (w << 16)); }
 
 // The norm of the row held in v (the residual sum h, already rounded to BF16), in place, unrounded:
 // KIND 0 (RMSNorm):   n = (h * r) * w,                r = rsqrt(sum(h^2) / D + eps)
 // KIND 1 (LayerNorm): n = ((h - mu) * r) * w + b,     mu = sum(h) / D, r = rsqrt(sum((h - mu)^2) / D + eps)
-// w / b optional (NULL = 1 / 0), FP32 or (WBF16) BF16; ms / mh (BF16, NULL = none): n = n * (1 + ms) + mh.
+// w / b optional (NULL = 1 / 0), FP32 or (WBF16) BF16, in global memory or a shared-memory copy; ms / mh (BF16,
+// NULL = none): n = n * (1 + ms) + mh, the thread's first chunk from m0 when m0.on.
 // Every thread of the block must call it (it synchronizes).
 template <int KIND, bool WBF16>
 __device__ __forceinline__ void norm_chunks(float (&v)[kNormMaxChunks][16], int D, const void* w, const void* b,
-                                            const u16* ms, const u16* mh, float eps, float* red) {
+                                            const u16* ms, const u16* mh, float eps, float* red, const ModChunk& m0) {
     const int nch = D >> 4;
     float part = 0.f;
 #pragma unroll
@@ -109,7 +132,11 @@ __device__ __forceinline__ void norm_chunks(float (&v)[kNormMaxChunks][16], int 
                 float t = KIND == 0 ? v[k][i] * r : (v[k][i] - mu) * r;
                 if (w) t = t * ldp<WBF16>(w, j);
                 if (b) t = t + ldp<WBF16>(b, j);
-                if (ms) t = t * (1.f + bf2f(__ldg(ms + j))) + bf2f(__ldg(mh + j));
+                if (ms) {
+                    const float a = k == 0 && m0.on ? bf_half(m0.s[i >> 1], i) : bf2f(__ldg(ms + j));
+                    const float c = k == 0 && m0.on ? bf_half(m0.h[i >> 1], i) : bf2f(__ldg(mh + j));
+                    t = t * (1.f + a) + c;
+                }
                 v[k][i] = t;
             }
         }

@@ -181,6 +181,14 @@ __device__ __forceinline__ void load_signs16(const i8* p, float* sg) {
     for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
 }
 
+// The same for a vector that may be a shared-memory copy (stage_const): plain, generic loads.
+__device__ __forceinline__ void load_signs16_any(const i8* p, float* sg) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    const u32 w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
+}
+
 __device__ __forceinline__ void load_f16x(const float* p, float* v) {
     const float4* f = reinterpret_cast<const float4*>(p);
 #pragma unroll
@@ -190,13 +198,23 @@ __device__ __forceinline__ void load_f16x(const float* p, float* v) {
     }
 }
 
+__device__ __forceinline__ void load_f16x_any(const float* p, float* v) {
+    const float4* f = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 a = f[q];
+        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+    }
+}
+
 // Scaled accumulator inputs z = SCALE(acc): I32 ((float)a * s) * rs, F32 a, BF16 bf2f(a) * rs (kernels.py:545).
+// rs may be a shared-memory copy (stage_const).
 template <int AT>
 __device__ __forceinline__ void load_scaled16(const void* acc, size_t idx, float s, const float* rs, float* v) {
     if (AT == TCQ_DT_I32) {
         const int4* a4 = reinterpret_cast<const int4*>(reinterpret_cast<const int*>(acc) + idx);
         float r[16];
-        load_f16x(rs, r);
+        load_f16x_any(rs, r);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int4 a = __ldg(a4 + q);
@@ -209,7 +227,7 @@ __device__ __forceinline__ void load_scaled16(const void* acc, size_t idx, float
         load_f16x(reinterpret_cast<const float*>(acc) + idx, v);
     } else {
         float r[16];
-        load_f16x(rs, r);
+        load_f16x_any(rs, r);
         load16<TCQ_DT_BF16>(reinterpret_cast<const u16*>(acc) + idx, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k) v[k] = v[k] * r[k];

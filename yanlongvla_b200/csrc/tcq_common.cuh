@@ -111,6 +111,25 @@ TCQ_HD void prefetch_l2_bulk(const void* p, unsigned bytes) {
 TCQ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TCQ_HD void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Shared-memory copy of a layer-constant vector (a parameter no kernel of the stream writes: signs, row scales,
+// biases, norm weights), made by the whole block BEFORE pdl_wait(): a launched-early kernel then reads its constants
+// from shared memory instead of paying a global round trip for each of them after the dependency is released.
+// `bytes` is a multiple of 16 and `sp` advances by it (so it stays 16-byte aligned). Returns a generic pointer to the
+// copy, or src itself when src is NULL or `on` is false; either way it must be read with plain loads (never __ldg).
+// The caller synchronizes the block before the copy is read.
+TCQ_HD const void* stage_const(char*& sp, const void* src, int bytes, bool on) {
+    if (!src || !on) return src;
+    char* dst = sp;
+    sp += bytes;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        for (int i = threadIdx.x; i < (bytes >> 4); i += blockDim.x)
+            reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    } else {
+        for (int i = threadIdx.x; i < bytes; i += blockDim.x) dst[i] = __ldg(reinterpret_cast<const char*>(src) + i);
+    }
+    return dst;
+}
+
 // ---------------------------------------------------------------------------------------------------- host helpers
 #define TCQ_CHECK_LAUNCH()                                        \
     do {                                                          \
@@ -119,3 +138,23 @@ TCQ_HD void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_depend
     } while (0)
 
 static inline bool tcq_aligned(const void* p, size_t a) { return (((uintptr_t)p) & (a - 1)) == 0; }
+
+// Streaming multiprocessors of the current device (queried once per translation unit; 148, a B200's, if the query
+// fails).
+static inline int tcq_sm_count() {
+    static int n = 0;
+    if (n <= 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            n <= 0)
+            n = 148;
+    }
+    return n;
+}
+
+// Row kernels (one block per token row) stage their layer constants in shared memory (stage_const) when the launch
+// is latency-bound: at most a few rows per SM, so the extra shared memory costs no occupancy. Many-row launches read
+// the constants through L1, where the blocks of an SM share them.
+static inline bool tcq_stage_rows(int rows, size_t const_bytes, size_t max_bytes) {
+    return const_bytes <= max_bytes && rows <= 4 * tcq_sm_count();
+}
