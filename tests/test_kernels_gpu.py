@@ -171,6 +171,25 @@ def test_rotate(K, T, D):
     _eq(n(yb), O.f32_to_bf16(O.rotate(x, sg, 'bf16')), 'rotate bf16 out')
 
 
+def test_bf16_rounding_special_values(K):
+    """BF16 outputs follow the reference's scalar rounding for every FP32 input class: overflow to infinity,
+    infinities, NaN (-> 0x7fc0, whatever NaN the arithmetic produced), subnormals and signed zeros."""
+    D = 64
+    sg = np.where(cases.rng('special.sg', D).random(D) < 0.5, -1, 1).astype(np.int8)
+    x = cases.rng('special.x', D).standard_normal((6, D)).astype(np.float32)
+    x[1, 5] = np.nan
+    x[2, 7] = np.inf
+    x[3, :] = 3.0e38                                   # butterflies overflow to +-inf, inf - inf gives NaN
+    x[4, :] *= np.float32(1e-39)                       # subnormal sums and outputs
+    x[5, :] = 0.0
+    x[5, ::3] = -0.0
+    for inverse in (False, True):
+        y = K.rotate(t(x), t(sg), inverse=inverse, out_dtype=torch.bfloat16)
+        with np.errstate(all='ignore'):
+            want = O.f32_to_bf16(O.rotate(x, sg, 'f32', inverse=inverse))
+        _eq(n(y), want, f'rotate bf16 special values (inverse={inverse})')
+
+
 @pytest.mark.parametrize('dt', ['bf16', 'f16', 'f32'])
 @pytest.mark.parametrize('Kd', [16, 48, 1152, 4304, 12288, 16384])
 def test_pre_dtypes_and_widths(K, dt, Kd):

@@ -16,7 +16,7 @@ using namespace tcq;
 // Modulation vectors: row group g = row / mod_rows (rows of one sample), row stride ld_mod.
 // stage: the norm weights are copied into shared memory before the dependency wait (dynamic shared memory holds
 // them); the modulation values of the first chunk are loaded with x and y.
-template <int KIND, bool WBF16>
+template <int KIND, bool WBF16, int NC>
 __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
                                                  u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
                                                  const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
@@ -36,24 +36,22 @@ __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, cons
     ModChunk m0{};
     if (ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0 && (int)threadIdx.x < nch)
         load_mod_chunk(m0, ms + 16 * threadIdx.x, mh + 16 * threadIdx.x);
-    float v[kNormMaxChunks][16];
+    float v[NC][16];
 #pragma unroll
-    for (int k = 0; k < kNormMaxChunks; ++k) {
+    for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
             load_bf16x16(x + base + 16 * c, v[k]);
             if (y) {
                 float t[16];
                 load_bf16x16(y + base + 16 * c, t);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) v[k][i] = bf16_round(v[k][i] + t[i]);
-                if (hout) store_bf16x16(hout + base + 16 * c, v[k]);
+                add_round_chunk(v[k], t, hout ? hout + base + 16 * c : nullptr);
             }
         }
     }
-    norm_chunks<KIND, WBF16>(v, D, ws, bs, ms, mh, eps, red, m0);
+    norm_chunks<KIND, WBF16, NC>(v, D, ws, bs, ms, mh, eps, red, m0);
 #pragma unroll
-    for (int k = 0; k < kNormMaxChunks; ++k) {
+    for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) store_bf16x16(nout + base + 16 * c, v[k]);
     }
@@ -112,7 +110,11 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
         return TCQ_ERR_ALIGN;
     const int T = norm_threads(D);
     const bool wb = wb_dtype == TCQ_DT_BF16;
-    auto kern = kind == 0 ? (wb ? k_addnorm<0, true> : k_addnorm<0, false>) : (wb ? k_addnorm<1, true> : k_addnorm<1, false>);
+    const bool one = (D >> 4) <= 512;     // one 16-element chunk per thread (T = D / 16 threads)
+    auto kern = one ? (kind == 0 ? (wb ? k_addnorm<0, true, 1> : k_addnorm<0, false, 1>)
+                                 : (wb ? k_addnorm<1, true, 1> : k_addnorm<1, false, 1>))
+                    : (kind == 0 ? (wb ? k_addnorm<0, true, kNormMaxChunks> : k_addnorm<0, false, kNormMaxChunks>)
+                                 : (wb ? k_addnorm<1, true, kNormMaxChunks> : k_addnorm<1, false, kNormMaxChunks>));
     const int cbytes = ((w ? 1 : 0) + (b ? 1 : 0)) * (wb ? 2 : 4) * D;
     const int stage = cbytes > 0 && tcq_stage_rows(M, cbytes, kStageMaxBytes);
     return launch_rows(kern, M, T, stage ? cbytes : 0, stream, (const u16*)x, (const u16*)y, (u16*)h, (u16*)out, w, b,

@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(512) k_pre(const void* __restrict__ x, const i
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
     float mx = 0.f;
-    row_walsh(buf, K,
+    row_walsh16(buf, K,
               [&](int c, float* v) {
                   float sg[16];
                   load16<DT>(xr + (size_t)16 * c * es, v);
@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(512) k_pre(const void* __restrict__ x, const i
 #pragma unroll
                   for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
               },
+              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
               [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
 }
@@ -51,7 +52,7 @@ __global__ void __launch_bounds__(512) k_pre2(const u16* __restrict__ g, const u
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * K;
     float mx = 0.f;
-    row_walsh(buf, K,
+    row_walsh16(buf, K,
               [&](int c, float* v) {
                   float gv[16], uv[16], sg[16];
                   load16<TCQ_DT_BF16>(g + base + 16 * c, gv);
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(512) k_pre2(const u16* __restrict__ g, const u
 #pragma unroll
                   for (int k = 0; k < 16; ++k) v[k] = bf2f(f2bf(gv[k] * uv[k])) * sg[k];
               },
+              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
               [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
 }
@@ -73,13 +75,22 @@ __global__ void __launch_bounds__(512) k_pre_h(const void* __restrict__ x, const
     const int tok = blockIdx.x;
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
-    row_walsh(buf, K,
+    row_walsh16(buf, K,
               [&](int c, float* v) {
                   float sg[16];
                   load16<DT>(xr + (size_t)16 * c * es, v);
                   load_signs16(su + 16 * c, sg);
 #pragma unroll
                   for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
+              },
+              [&](int i0, const float* v) {
+                  u32 w[8];
+                  pack_bf16x16(v, w);
+                  if (h) store16_bf16_any(h + (size_t)tok * K + i0, w);
+                  if (hT) {
+#pragma unroll
+                      for (int k = 0; k < 16; ++k) hT[(size_t)(i0 + k) * ldh + tok] = (u16)((k & 1) ? (w[k >> 1] >> 16) : (w[k >> 1] & 0xffffu));
+                  }
               },
               [&](int i, float v) {
                   const u16 b = f2bf(v);
@@ -97,7 +108,7 @@ __global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, cons
     const int tok = blockIdx.x;
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * D * es;
-    row_walsh(buf, D,
+    row_walsh16(buf, D,
               [&](int c, float* v) {
                   load16<DT>(xr + (size_t)16 * c * es, v);
                   if (!inverse) {
@@ -105,6 +116,26 @@ __global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, cons
                       load_signs16(sg + 16 * c, s16);
 #pragma unroll
                       for (int k = 0; k < 16; ++k) v[k] = v[k] * s16[k];
+                  }
+              },
+              [&](int i0, const float* vin) {
+                  float v[16];
+#pragma unroll
+                  for (int k = 0; k < 16; ++k) v[k] = vin[k];
+                  if (inverse) {
+                      float s16[16];
+                      load_signs16(sg + i0, s16);
+#pragma unroll
+                      for (int k = 0; k < 16; ++k) v[k] = v[k] * s16[k];
+                  }
+                  if (OT == TCQ_DT_F32) {
+                      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + (size_t)tok * D + i0);
+#pragma unroll
+                      for (int q = 0; q < 4; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                  } else {
+                      u32 w[8];
+                      pack_bf16x16(v, w);
+                      store16_bf16(reinterpret_cast<u16*>(y) + (size_t)tok * D + i0, w);
                   }
               },
               [&](int i, float v) {
@@ -115,15 +146,32 @@ __global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, cons
 }
 
 // Epilogue of one layer on one token: SCALE(acc[base + i]) -> block Walsh -> * sv -> + bias -> BF16 (-> act).
-template <int AT, class Out>
+// out(i, b): one BF16 result; out16(i0, w): the 16 results of chunk i0 as 8 packed words (element i0 + k in the low
+// half of w[k / 2] for even k). sv / bias may be shared-memory copies.
+template <int AT, class Out, class Out16>
 __device__ __forceinline__ void post_row(float* buf, const void* acc, size_t base, float s, const float* rs, const i8* sv,
-                                         const float* bias, int N, Out out) {
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, s, rs ? rs + 16 * c : nullptr, v); },
-              [&](int i, float v) {
-                  v = v * (float)sv[i];
-                  if (bias) v = v + bias[i];
-                  out(i, f2bf(v));
-              });
+                                         const float* bias, int N, Out out, Out16 out16) {
+    row_walsh16(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, s, rs ? rs + 16 * c : nullptr, v); },
+                [&](int i0, const float* vin) {
+                    float v[16], sg[16];
+                    load_signs16_any(sv + i0, sg);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] = vin[k] * sg[k];
+                    if (bias) {
+                        float bb[16];
+                        load_f16x_any(bias + i0, bb);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) v[k] = v[k] + bb[k];
+                    }
+                    u32 w[8];
+                    pack_bf16x16(v, w);
+                    out16(i0, w);
+                },
+                [&](int i, float v) {
+                    v = v * (float)sv[i];
+                    if (bias) v = v + bias[i];
+                    out(i, f2bf(v));
+                });
 }
 
 template <int AT>
@@ -140,7 +188,8 @@ __global__ void __launch_bounds__(512) k_post(const void* __restrict__ acc, cons
     pdl_wait();
     const int tok = blockIdx.x;
     u16* yo = y + (size_t)tok * N;
-    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 b) { yo[i] = b; });
+    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 b) { yo[i] = b; },
+                 [&](int i0, const u32* w) { store16_bf16_any(yo + i0, w); });
 }
 
 // Several layers sharing the accumulator row. grid.y == 1: the layers one after another in one block (post3);
@@ -172,7 +221,17 @@ __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc
         u16* yo = (seg == 0 ? y0 : seg == 1 ? y1 : y2) + (size_t)tok * N;
         const bool act = act0 && seg == 0;
         post_row<AT>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rsc ? rsc + (c0 - cs) : nullptr, svc + (c0 - cs),
-                     biasc ? biasc + (c0 - cs) : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; });
+                     biasc ? biasc + (c0 - cs) : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; },
+                     [&](int i0, const u32* w) {
+                         if (act) {
+                             u32 a[8];
+#pragma unroll
+                             for (int k = 0; k < 8; ++k) a[k] = (u32)lut[w[k] & 0xffffu] | ((u32)lut[w[k] >> 16] << 16);
+                             store16_bf16_any(yo + i0, a);
+                         } else {
+                             store16_bf16_any(yo + i0, w);
+                         }
+                     });
     }
 }
 
@@ -185,7 +244,7 @@ __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc
 //                        tcq_add_norm; BF16(n) written to nout when given
 //   q / q4, scale        = pre(BF16(n), su) as k_pre on a BF16 input                             (su != NULL)
 // Each step is bit-identical to the separate kernel. Shared memory: N floats (Walsh buffer) + N BF16 (y, then n).
-template <int AT, int KIND, bool WBF16>
+template <int AT, int KIND, bool WBF16, int NC>
 __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                                const i8* __restrict__ sv, const float* __restrict__ bias, int lda, int col0,
                                                const u16* __restrict__ yg, const u16* __restrict__ x, u16* __restrict__ hout,
@@ -210,69 +269,80 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
     pdl_wait();
     const int tok = blockIdx.x, nch = N >> 4;
     const size_t base = (size_t)tok * N;
-    // The thread's first chunk of x (and of y / the modulation) is requested now, with the accumulators, so that the
-    // residual add and the norm do not wait on another global round trip.
+    // With staging on, the thread's first chunk of x (and of y / the modulation) is copied into shared memory
+    // asynchronously now, with the accumulator loads in flight, so that the residual add and the norm find it there
+    // (the copy area follows the constants: x, then y when added from a tensor, then the two modulation vectors).
     const bool first = (int)threadIdx.x < nch;
     const u16* ms = mscale ? mscale + (size_t)(tok / mod_rows) * ld_mod : nullptr;
     const u16* mh = mscale ? mshift + (size_t)(tok / mod_rows) * ld_mod : nullptr;
-    uint4 x0a = make_uint4(0, 0, 0, 0), x0b = x0a, y0a = x0a, y0b = x0a;
-    ModChunk m0{};
-    if (first) {
-        const uint4* xp = reinterpret_cast<const uint4*>(x + base + 16 * threadIdx.x);
-        x0a = __ldg(xp);
-        x0b = __ldg(xp + 1);
-        if (!acc && yg) {
-            const uint4* yp = reinterpret_cast<const uint4*>(yg + base + 16 * threadIdx.x);
-            y0a = __ldg(yp);
-            y0b = __ldg(yp + 1);
+    const bool ycopy = !acc && yg, mcopy = ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0;
+    u16* xs = reinterpret_cast<u16*>(sp);
+    u16* ys = xs + N;
+    u16* mss = ys + (ycopy ? N : 0);
+    u16* mhs = mss + N;
+    if (on && first) {
+        const int o = 16 * threadIdx.x;
+        cp_async16(xs + o, x + base + o);
+        cp_async16(xs + o + 8, x + base + o + 8);
+        if (ycopy) {
+            cp_async16(ys + o, yg + base + o);
+            cp_async16(ys + o + 8, yg + base + o + 8);
         }
-        if (ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0) load_mod_chunk(m0, ms + 16 * threadIdx.x, mh + 16 * threadIdx.x);
+        if (mcopy) {
+            cp_async16(mss + o, ms + o);
+            cp_async16(mss + o + 8, ms + o + 8);
+            cp_async16(mhs + o, mh + o);
+            cp_async16(mhs + o + 8, mh + o + 8);
+        }
     }
     if (acc)                                        // ends with a block barrier: yb complete
-        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 v) { yb[i] = v; });
-    float v[kNormMaxChunks][16];
+        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 v) { yb[i] = v; },
+                     [&](int i0, const u32* w) { store16_bf16(yb + i0, w); });
+    ModChunk m0{};
+    if (on) {
+        cp_async_wait_all();                        // this thread's copies (it reads only its own chunk)
+        if (mcopy && first) load_mod_chunk_smem(m0, mss + 16 * threadIdx.x, mhs + 16 * threadIdx.x);
+    }
+    float v[NC][16];
 #pragma unroll
-    for (int k = 0; k < kNormMaxChunks; ++k) {
+    for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
-            if (k == 0) unpack_bf16x16(x0a, x0b, v[k]);
+            if (k == 0 && on) load_bf16x16_any(xs + 16 * c, v[k]);
             else load_bf16x16(x + base + 16 * c, v[k]);
             if (acc || yg) {
                 float t[16];
-                if (acc) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) t[i] = bf2f(yb[16 * c + i]);
-                } else if (k == 0) {
-                    unpack_bf16x16(y0a, y0b, t);
-                } else {
-                    load_bf16x16(yg + base + 16 * c, t);
-                }
-#pragma unroll
-                for (int i = 0; i < 16; ++i) v[k][i] = bf16_round(v[k][i] + t[i]);
-                if (hout) store_bf16x16(hout + base + 16 * c, v[k]);
+                if (acc) load_bf16x16_any(yb + 16 * c, t);
+                else if (k == 0 && on) load_bf16x16_any(ys + 16 * c, t);
+                else load_bf16x16(yg + base + 16 * c, t);
+                add_round_chunk(v[k], t, hout ? hout + base + 16 * c : nullptr);
             }
         }
     }
-    norm_chunks<KIND, WBF16>(v, N, wc, bc, ms, mh, eps, red, m0);   // synchronizes: every thread is past its reads of yb
+    norm_chunks<KIND, WBF16, NC>(v, N, wc, bc, ms, mh, eps, red, m0);   // synchronizes: every thread is past its reads of yb
 #pragma unroll
-    for (int k = 0; k < kNormMaxChunks; ++k) {
+    for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
-            if (nout) store_bf16x16(nout + base + 16 * c, v[k]);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) yb[16 * c + i] = f2bf(v[k][i]);
+            u32 wn[8];
+            pack_bf16x16(v[k], wn);
+            if (nout) store16_bf16(nout + base + 16 * c, wn);
+            store16_bf16(yb + 16 * c, wn);
         }
     }
     if (!su) return;
     __syncthreads();
     float mx = 0.f;
-    row_walsh(buf, N,
+    row_walsh16(buf, N,
               [&](int c, float* vv) {
                   float sg[16];
                   load_signs16_any(suc + 16 * c, sg);
+                  float nb[16];
+                  load_bf16x16_any(yb + 16 * c, nb);
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) vv[i] = bf2f(yb[16 * c + i]) * sg[i];
+                  for (int i = 0; i < 16; ++i) vv[i] = nb[i] * sg[i];
               },
+              [&](int i0, const float* vv) { store_chunk(buf, i0, vv, mx); },
               [&](int i, float val) { buf[swz(i)] = val; mx = fmaxf(mx, fabsf(val)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
@@ -301,12 +371,12 @@ __global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, cons
     row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
               [&](int i, float v) { gb[i] = lut[f2bf(v * (float)svc[i])]; });
     row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + N + 16 * c, st, rsc ? rsc + N + 16 * c : nullptr, v); },
-              [&](int i, float v) {
-                  const u16 u = f2bf(v * (float)svc[N + i]);
-                  buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)suc[i];
-              });
+                [&](int i, float v) {
+                    const u16 u = f2bf(v * (float)svc[N + i]);
+                    buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)suc[i];
+                });
     float mx = 0.f;
-    row_walsh(buf, N,
+    row_walsh16(buf, N,
               [&](int c, float* v) {
                   const float4* b4 = reinterpret_cast<const float4*>(buf);
 #pragma unroll
@@ -315,6 +385,7 @@ __global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, cons
                       v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
                   }
               },
+              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
               [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
@@ -340,13 +411,13 @@ __global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, cons
     const size_t base = (size_t)tok * lda;
     const float st = s ? s[tok] : 1.f;
     row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
-              [&](int i, float v) {
-                  v = v * (float)svc[i];
-                  if (biasc) v = v + biasc[i];
-                  buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)suc[i];
-              });
+                [&](int i, float v) {
+                    v = v * (float)svc[i];
+                    if (biasc) v = v + biasc[i];
+                    buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)suc[i];
+                });
     float mx = 0.f;
-    row_walsh(buf, N,
+    row_walsh16(buf, N,
               [&](int c, float* v) {
                   const float4* b4 = reinterpret_cast<const float4*>(buf);
 #pragma unroll
@@ -355,6 +426,7 @@ __global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, cons
                       v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
                   }
               },
+              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
               [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
@@ -573,12 +645,18 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
     // Layer constants staged by the kernel (the same set, in bytes): rs (I32 accumulators), bias, sv, w, b, su.
     const size_t cb = (acc ? (size_t)(i32 ? 4 * N : 0) + (bias ? 4 * N : 0) + N : 0) + (size_t)(w ? 1 : 0) * (wb ? 2 : 4) * N +
                       (size_t)(b ? 1 : 0) * (wb ? 2 : 4) * N + (su ? N : 0);
-    const int stage = tcq_stage_rows(M, cb, kStageMaxBytes);
-    const size_t smem = (size_t)6 * N + (stage ? cb : 0);
-    auto kern = kind == 0 ? (i32 ? (wb ? k_chain<TCQ_DT_I32, 0, true> : k_chain<TCQ_DT_I32, 0, false>)
-                                 : (wb ? k_chain<TCQ_DT_F32, 0, true> : k_chain<TCQ_DT_F32, 0, false>))
-                          : (i32 ? (wb ? k_chain<TCQ_DT_I32, 1, true> : k_chain<TCQ_DT_I32, 1, false>)
-                                 : (wb ? k_chain<TCQ_DT_F32, 1, true> : k_chain<TCQ_DT_F32, 1, false>));
+    // With staging on, also the copy area of x (and y, the two modulation vectors) for the first chunks.
+    const size_t pb = (size_t)2 * N * (1 + (!acc && y ? 1 : 0) + (mod_scale ? 2 : 0));
+    const int stage = tcq_stage_rows(M, cb, kStageMaxBytes) && (size_t)6 * N + cb + pb <= (size_t)kStageMaxSmem;
+    const size_t smem = (size_t)6 * N + (stage ? cb + pb : 0);
+    // One 16-element chunk per thread up to N = 8192 (T = N / 16 threads); wider rows hold kNormMaxChunks per thread.
+    const bool one = (N >> 4) <= 512;
+#define TCQ_CHAIN(AT_, K_, WB_) (one ? k_chain<AT_, K_, WB_, 1> : k_chain<AT_, K_, WB_, kNormMaxChunks>)
+    auto kern = kind == 0 ? (i32 ? (wb ? TCQ_CHAIN(TCQ_DT_I32, 0, true) : TCQ_CHAIN(TCQ_DT_I32, 0, false))
+                                 : (wb ? TCQ_CHAIN(TCQ_DT_F32, 0, true) : TCQ_CHAIN(TCQ_DT_F32, 0, false)))
+                          : (i32 ? (wb ? TCQ_CHAIN(TCQ_DT_I32, 1, true) : TCQ_CHAIN(TCQ_DT_I32, 1, false))
+                                 : (wb ? TCQ_CHAIN(TCQ_DT_F32, 1, true) : TCQ_CHAIN(TCQ_DT_F32, 1, false)));
+#undef TCQ_CHAIN
     return launch(kern, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, lda, col0, (const u16*)y, (const u16*)x,
                   (u16*)h, (u16*)n, w, b, (const u16*)mod_scale, (const u16*)mod_shift, mod_rows, ld_mod, eps, (const i8*)su, q,
                   (int*)q4, scale, ldq, N, stage);

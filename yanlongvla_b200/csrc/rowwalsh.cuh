@@ -33,16 +33,20 @@ __device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bo
 }
 
 // ld16(c, v): the 16 inputs of chunk c (indices 16c .. 16c+15). fin(i, value): called exactly once per index with the
-// finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]).
-// Ends with a __syncthreads() so that values fin stored to buf are visible to the whole block.
+// finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]). fin16(i0, v): the
+// same for the 16 finished values of a whole chunk i0 .. i0+15 at once (blocks of up to 512, finished in registers),
+// so that callers can load their per-index operands and store their results 16 bytes at a time.
+// Ends with a __syncthreads() so that values fin / fin16 stored to buf are visible to the whole block.
 //
 // Stages h = 1..8 run in registers on a thread's 16 contiguous inputs; h = 16..256 across the 32 lanes of a warp,
 // which hold 32 consecutive chunks (lane partner = lane ^ h/16: the lower lane keeps a + b, the upper b' = a - b, the
-// reference's operands in its order); blocks of up to 512 are then done. Wider blocks finish with radix-16 passes
-// through shared memory at stride 512 (and 8192). Threads per row are a multiple of 32, so a warp's chunks are
-// consecutive; blocks are aligned to their width, so a stage never pairs chunks of different blocks.
-template <class Ld16, class Fin>
-__device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
+// reference's operands in its order; both as one rounding of (+-1) * own + partner); blocks of up to 512 are then
+// done. Wider blocks finish with radix-16 passes through shared memory at stride 512 (and 8192). Threads per row are
+// a multiple of 32, so a warp's chunks are consecutive; blocks are aligned to their width, so a stage never pairs
+// chunks of different blocks. The cross-lane stages are a rolled loop: row kernels run once per launch and are bound
+// by instruction fetch, not by the loop overhead.
+template <class Ld16, class Fin16, class Fin>
+__device__ __forceinline__ void row_walsh16(float* buf, int K, Ld16 ld16, Fin16 fin16, Fin fin) {
     const int nch = K >> 4, lane = threadIdx.x & 31;
     for (int c0 = threadIdx.x - lane; c0 < nch; c0 += blockDim.x) {        // warp-uniform
         const int c = c0 + lane;
@@ -56,15 +60,15 @@ __device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin)
 #pragma unroll
             for (int k = 0; k < 16; ++k) v[k] = 0.f;
         }
-#pragma unroll
-        for (int st = 0; st < 5; ++st) {
-            const int hc = 1 << st;                                            // stage h = 16 hc
+#pragma unroll 1
+        for (int hc = 1; hc < 32; hc <<= 1) {                                 // stage h = 16 hc
             if (!__any_sync(0xffffffffu, w > 16 * hc)) break;
-            const bool upper = (lane & hc) != 0, act = w > 16 * hc;
+            const bool act = w > 16 * hc;
+            const float sg = (lane & hc) ? -1.f : 1.f;                         // upper lane: partner - own
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
-                if (act) v[k] = upper ? p - v[k] : v[k] + p;
+                if (act) v[k] = __fmaf_rn(sg, v[k], p);
             }
         }
         if (c < nch) {
@@ -72,7 +76,8 @@ __device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin)
             if (w <= 512) {
                 const float sc = wscale(w);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) fin(i0 + k, v[k] * sc);
+                for (int k = 0; k < 16; ++k) v[k] = v[k] * sc;
+                fin16(i0, v);
             } else {
                 float4* b4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
@@ -105,6 +110,25 @@ __device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin)
     }
 }
 
+template <class Ld16, class Fin>
+__device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
+    row_walsh16(buf, K, ld16, [&](int i0, const float* v) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) fin(i0 + k, v[k]);
+    }, fin);
+}
+
+// fin16 of a pass whose result is the finished row in buf (at swz(i)) plus its absolute maximum: four 16-byte stores.
+__device__ __forceinline__ void store_chunk(float* buf, int i0, const float* v, float& mx) {
+    float4* b4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx = fmaxf(mx, fabsf(v[4 * q + k]));
+    }
+}
+
 __device__ __forceinline__ float block_max(float mx, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -129,20 +153,50 @@ __device__ __forceinline__ void quantize_store(const float* buf, float mx, float
     mx = block_max(mx, red);
     const float s = mx > 0.f ? mx / 127.f : 1.f;
     if (threadIdx.x == 0) scale[tok] = s;
+    // Four values (one q4 word) per step, in a rolled loop: the division's code is fetched once, not sixteen times.
     const float4* b4 = reinterpret_cast<const float4*>(buf);
     for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
-        u32 w[4];
-#pragma unroll
+#pragma unroll 1
         for (int g = 0; g < 4; ++g) {
             const float4 v = b4[swz(16 * c + 4 * g) >> 2];
-            w[g] = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
-                   ((u32)(q8(v.w, s) & 0xff) << 24);
+            const u32 w = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
+                          ((u32)(q8(v.w, s) & 0xff) << 24);
+            if (q) reinterpret_cast<u32*>(q + (size_t)tok * K + 16 * c)[g] = w;
+            if (q4) q4[(size_t)(4 * c + g) * ldq + tok] = (int)w;
         }
-        if (q) *reinterpret_cast<uint4*>(q + (size_t)tok * K + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
-        if (q4) {
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------- chunk I/O
+// The same for a destination of unknown alignment (a caller's output view): 16-byte stores when p allows them.
+__device__ __forceinline__ void store16_bf16_any(u16* p, const u32* w) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        store16_bf16(p, w);
+    } else {
 #pragma unroll
-            for (int g = 0; g < 4; ++g) q4[(size_t)(4 * c + g) * ldq + tok] = (int)w[g];
+        for (int k = 0; k < 8; ++k) {
+            p[2 * k] = (u16)(w[k] & 0xffffu);
+            p[2 * k + 1] = (u16)(w[k] >> 16);
         }
+    }
+}
+
+// 16 finished FP32 values of chunk i0 into the row buffer at swz(i0 + k): four 16-byte stores.
+__device__ __forceinline__ void store16_f32_swz(float* buf, int i0, const float* v) {
+    float4* b4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// 16 BF16 values from p (16-byte aligned, global or shared; generic loads).
+__device__ __forceinline__ void load_bf16x16_any(const u16* p, float* v) {
+    const uint4* u = reinterpret_cast<const uint4*>(p);
+    const uint4 a = u[0], b = u[1];
+    const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
     }
 }
 

@@ -29,6 +29,38 @@ TCQ_HD u16 f2bf(float f) {
     return (u16)(u >> 16);
 }
 
+// Two values at once: the hardware round-to-nearest-even conversion (identical to f2bf for every non-NaN input,
+// infinities, overflow to infinity and subnormals included), lo in the low half; a pair holding a NaN is redone with
+// f2bf for the NaN rule.
+TCQ_HD u32 f2bf2(float lo, float hi) {
+    u32 r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    if (lo != lo || hi != hi) r = (u32)f2bf(lo) | ((u32)f2bf(hi) << 16);
+    return r;
+}
+
+// 16 values as BF16, element k in the low (even k) or high (odd k) half of w[k / 2].
+TCQ_HD void pack_bf16x16(const float* v, u32* w) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = f2bf2(v[2 * k], v[2 * k + 1]);
+}
+
+// The 16 packed values back to FP32 (exact).
+TCQ_HD void unpack_bf16w(const u32* w, float* v) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+}
+
+// Two 16-byte stores of 8 packed words (p 16-byte aligned: global or shared).
+TCQ_HD void store16_bf16(u16* p, const u32* w) {
+    uint4* u = reinterpret_cast<uint4*>(p);
+    u[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    u[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 TCQ_HD float h2f(u16 h) {
     float f;
     asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
@@ -110,6 +142,13 @@ TCQ_HD void prefetch_l2_bulk(const void* p, unsigned bytes) {
 // predecessor drains; it must call pdl_wait() before touching anything the predecessor writes.
 TCQ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TCQ_HD void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Asynchronous 16-byte global -> shared copy (L2 only), both addresses 16-byte aligned; the issuing thread sees the
+// data after cp_async_wait_all() (other threads after a block barrier as well).
+TCQ_HD void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((u32)__cvta_generic_to_shared(smem)), "l"(gmem) : "memory");
+}
+TCQ_HD void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Shared-memory copy of a layer-constant vector (a parameter no kernel of the stream writes: signs, row scales,
 // biases, norm weights), made by the whole block BEFORE pdl_wait(): a launched-early kernel then reads its constants

@@ -258,7 +258,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         for (int m = 0; m < M; ++m) {
             const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
             float mx = 0.f;
-            row_walsh(sbuf, K,
+            row_walsh16(sbuf, K,
                       [&](int cc, float* v) {
                           float sg[16];
                           if (xdt == TCQ_DT_BF16) load16<TCQ_DT_BF16>(xr + (size_t)16 * cc * es, v);
@@ -268,6 +268,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
 #pragma unroll
                           for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
                       },
+                      [&](int i0, const float* v) { store_chunk(sbuf, i0, v, mx); },
                       [&](int i, float v) { sbuf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
             quantize_store(sbuf, mx, red, nullptr, sq4, ss, m, K, M);
             __syncthreads();                       // sbuf is rewritten by the next row; sq4 / ss complete
