@@ -98,3 +98,44 @@ def test_chain_norm_pre_without_add(K):
     q, sc = torch.empty_like(q_ref), torch.empty_like(sc_ref)
     h, n = K.chain(x, 'rms', w, None, 1e-6, su=su, q=q, scale=sc)
     assert h.data_ptr() == x.data_ptr() and torch.equal(n, n_ref) and torch.equal(q, q_ref) and torch.equal(sc, sc_ref)
+
+
+@pytest.mark.parametrize('kind', ['rms', 'ln'])
+@pytest.mark.parametrize('N', [1152, 1536, 2048])
+def test_rows_do_not_depend_on_launch_size(K, kind, N):
+    """A few rows run with 4-element chunks per thread, many rows with 16 (more threads per row only while the launch
+    is small); the norm's sum order is the same for both, so a row's results must not change with the row count."""
+    g = torch.Generator(device='cuda').manual_seed(N + (1 if kind == 'ln' else 0))
+    few, many = 5, 1200
+    acc = torch.randint(-2 ** 20, 2 ** 20, (few, N), dtype=torch.int32, device='cuda', generator=g)
+    s = torch.rand(few, device='cuda', generator=g) * 1e-3 + 1e-4
+    rs = torch.rand(N, device='cuda', generator=g) * 1e-2 + 1e-3
+    sv, su = _signs(N, g), _signs(N, g)
+    x = torch.randn(few, N, device='cuda', generator=g).bfloat16()
+    w = (torch.rand(N, device='cuda', generator=g) + 0.5).bfloat16()
+    nb = (torch.randn(N, device='cuda', generator=g) * 0.1).bfloat16() if kind == 'ln' else None
+    bias = torch.randn(N, device='cuda', generator=g) * 0.1
+    eps = 1e-6 if kind == 'rms' else 1e-5
+    rep = many // few
+
+    def run(a, sc, xx):
+        M = xx.shape[0]
+        y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+        K.post(a, sc, rs, sv, bias, y)
+        h1, n1 = K.add_norm(xx, y, w, nb, eps, kind)
+        q1 = torch.empty(M, N, dtype=torch.int8, device='cuda')
+        sc1 = torch.empty(M, device='cuda')
+        K.pre(n1, su, q=q1, scale=sc1)
+        q2 = torch.empty_like(q1)
+        sc2 = torch.empty_like(sc1)
+        h2, n2 = K.chain(xx, kind, w, nb, eps, acc=a, s=sc, rs=rs, sv=sv, bias=bias, su=su, q=q2, scale=sc2)
+        return [y, h1, n1, q1, sc1, h2, n2, q2, sc2]
+
+    small = run(acc, s, x)
+    large = run(acc.repeat(rep, 1), s.repeat(rep), x.repeat(rep, 1))
+    for a, b in zip(small, large):
+        assert torch.equal(a, b[:few])
+    # the fused chain equals its decomposition at both sizes
+    for out in (small, large):
+        assert torch.equal(out[5], out[1]) and torch.equal(out[6], out[2])
+        assert torch.equal(out[7], out[3]) and torch.equal(out[8], out[4])

@@ -1,9 +1,9 @@
 // Row kernels for the policy's glue around the quantized layers: residual add + RMSNorm / LayerNorm (+ the DiT's
 // AdaLN modulation) in one pass, and the rotary position embedding.
 //
-// One thread block per token row. A thread owns 16-element chunks c = threadIdx.x + k * blockDim.x of the row and
-// keeps them in registers; row sums are taken in a fixed order (each thread's elements in index order, then a
-// butterfly over the warp, then the warps' sums in warp order), so a row's result does not depend on timing.
+// One thread block per token row. A thread owns chunks c = threadIdx.x + k * blockDim.x of 4 or 16 elements of the
+// row and keeps them in registers; row sums are taken in a fixed order (each thread's elements in index order,
+// then a butterfly over the warp, then the warps' sums in warp order), so a row's result does not depend on timing.
 // The policy runs every runtime (the PyTorch reference runtime included) through these kernels, so the runtimes
 // agree bit for bit; tests compare them with a PyTorch FP32 restatement within BF16 rounding.
 #include "rownorm.cuh"
@@ -16,8 +16,8 @@ using namespace tcq;
 // Modulation vectors: row group g = row / mod_rows (rows of one sample), row stride ld_mod.
 // stage: the norm weights are copied into shared memory before the dependency wait (dynamic shared memory holds
 // them); the modulation values of the first chunk are loaded with x and y.
-template <int KIND, bool WBF16, int NC>
-__global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
+template <int KIND, bool WBF16, int NC, int CH>
+__global__ void __launch_bounds__(512, 1) k_addnorm(const u16* __restrict__ x, const u16* __restrict__ y, u16* __restrict__ hout,
                                                  u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
                                                  const u16* __restrict__ mscale, const u16* __restrict__ mshift, int mod_rows,
                                                  int ld_mod, float eps, int D, int stage) {
@@ -29,31 +29,35 @@ __global__ void __launch_bounds__(512) k_addnorm(const u16* __restrict__ x, cons
     const void* bs = stage_const(sp, b, (WBF16 ? 2 : 4) * D, stage != 0);
     __syncthreads();
     pdl_wait();
-    const int row = blockIdx.x, nch = D >> 4;
+    const int row = blockIdx.x, nch = D / CH;
     const size_t base = (size_t)row * D;
     const u16* ms = mscale ? mscale + (size_t)(row / mod_rows) * ld_mod : nullptr;
     const u16* mh = mscale ? mshift + (size_t)(row / mod_rows) * ld_mod : nullptr;
-    ModChunk m0{};
+    ModChunk<CH> m0{};
     if (ms && (((uintptr_t)ms | (uintptr_t)mh) & 15) == 0 && (int)threadIdx.x < nch)
-        load_mod_chunk(m0, ms + 16 * threadIdx.x, mh + 16 * threadIdx.x);
-    float v[NC][16];
+        load_mod_chunk<CH, true>(m0, ms + CH * threadIdx.x, mh + CH * threadIdx.x);
+    float v[NC][CH];
 #pragma unroll
     for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
-            load_bf16x16(x + base + 16 * c, v[k]);
+            loadc<TCQ_DT_BF16, CH>(x + base + CH * c, v[k]);
             if (y) {
-                float t[16];
-                load_bf16x16(y + base + 16 * c, t);
-                add_round_chunk(v[k], t, hout ? hout + base + 16 * c : nullptr);
+                float t[CH];
+                loadc<TCQ_DT_BF16, CH>(y + base + CH * c, t);
+                add_round_chunk<CH>(v[k], t, hout ? hout + base + CH * c : nullptr);
             }
         }
     }
-    norm_chunks<KIND, WBF16, NC>(v, D, ws, bs, ms, mh, eps, red, m0);
+    norm_chunks<KIND, WBF16, NC, CH>(v, D, ws, bs, ms, mh, eps, red, m0);
 #pragma unroll
     for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
-        if (c < nch) store_bf16x16(nout + base + 16 * c, v[k]);
+        if (c < nch) {
+            u32 wn[CH / 2];
+            pack_bf16c<CH>(v[k], wn);
+            store_bf16c<CH>(nout + base + CH * c, wn);
+        }
     }
 }
 
@@ -108,13 +112,15 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
     if (mod_scale && (mod_rows <= 0 || ld_mod < D)) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || !tcq_aligned(out, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)))
         return TCQ_ERR_ALIGN;
-    const int T = norm_threads(D);
+    // Chunks of 4 for a few rows up to 2048 wide (the sum order does not depend on the chunking), else 16: one chunk
+    // per thread up to 8192 wide.
+    const bool c4 = D <= 2048 && (long long)M * norm_threads(D, 4) <= (long long)tcq_sm_count() * 512;
+    const int T = norm_threads(D, c4 ? 4 : 16);
     const bool wb = wb_dtype == TCQ_DT_BF16;
-    const bool one = (D >> 4) <= 512;     // one 16-element chunk per thread (T = D / 16 threads)
-    auto kern = one ? (kind == 0 ? (wb ? k_addnorm<0, true, 1> : k_addnorm<0, false, 1>)
-                                 : (wb ? k_addnorm<1, true, 1> : k_addnorm<1, false, 1>))
-                    : (kind == 0 ? (wb ? k_addnorm<0, true, kNormMaxChunks> : k_addnorm<0, false, kNormMaxChunks>)
-                                 : (wb ? k_addnorm<1, true, kNormMaxChunks> : k_addnorm<1, false, kNormMaxChunks>));
+    auto pick = [&](auto k0, auto k1, auto k2) { return c4 ? k0 : D <= 8192 ? k1 : k2; };
+#define TCQ_ADDNORM(KD, WB) pick(k_addnorm<KD, WB, 1, 4>, k_addnorm<KD, WB, 1, 16>, k_addnorm<KD, WB, kNormMaxChunks, 16>)
+    auto kern = kind == 0 ? (wb ? TCQ_ADDNORM(0, true) : TCQ_ADDNORM(0, false)) : (wb ? TCQ_ADDNORM(1, true) : TCQ_ADDNORM(1, false));
+#undef TCQ_ADDNORM
     const int cbytes = ((w ? 1 : 0) + (b ? 1 : 0)) * (wb ? 2 : 4) * D;
     const int stage = cbytes > 0 && tcq_stage_rows(M, cbytes, kStageMaxBytes);
     return launch_rows(kern, M, T, stage ? cbytes : 0, stream, (const u16*)x, (const u16*)y, (u16*)h, (u16*)out, w, b,

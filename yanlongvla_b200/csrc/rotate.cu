@@ -7,6 +7,8 @@
 // registers; the later passes (stride 16, 256, 4096) go through shared memory in an XOR-swizzled layout that keeps
 // every 128-bit store and every 32-float warp access conflict-free. A radix-2^R pass performs exactly the additions
 // of R consecutive radix-2 stages in the same order, so the sums are bit-identical to the reference.
+#include <type_traits>
+
 #include "rownorm.cuh"
 #include "rowwalsh.cuh"
 #include "tcq_common.cuh"
@@ -18,8 +20,10 @@ using namespace tcq;
 constexpr int kMaxWidth = 16384;
 
 // ---------------------------------------------------------------------------------------------------- kernels
-template <int DT>
-__global__ void __launch_bounds__(512) k_pre(const void* __restrict__ x, const i8* __restrict__ su, int8_t* __restrict__ q,
+// CH: elements per thread chunk (4 or 16, see rowwalsh.cuh); the host picks it per launch (rows_ch) and launches
+// threads_for(K, CH) threads per row.
+template <int DT, int CH>
+__global__ void __launch_bounds__(512, 1) k_pre(const void* __restrict__ x, const i8* __restrict__ su, int8_t* __restrict__ q,
                                              int* __restrict__ q4, float* __restrict__ scale, int M, int K, int ldq) {
     extern __shared__ __align__(16) float buf[];
     __shared__ float red[32];
@@ -29,20 +33,21 @@ __global__ void __launch_bounds__(512) k_pre(const void* __restrict__ x, const i
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
     float mx = 0.f;
-    row_walsh16(buf, K,
-              [&](int c, float* v) {
-                  float sg[16];
-                  load16<DT>(xr + (size_t)16 * c * es, v);
-                  load_signs16(su + 16 * c, sg);
+    row_walshc<CH>(buf, K,
+                   [&](int c, float* v) {
+                       float sg[CH];
+                       loadc<DT, CH>(xr + (size_t)CH * c * es, v);
+                       load_signsc<CH, true>(su + CH * c, sg);
 #pragma unroll
-                  for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
-              },
-              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
-              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+                       for (int k = 0; k < CH; ++k) v[k] = v[k] * sg[k];
+                   },
+                   [&](int i0, const float* v) { store_chunk<CH>(buf, i0, v, mx); },
+                   [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
 }
 
-__global__ void __launch_bounds__(512) k_pre2(const u16* __restrict__ g, const u16* __restrict__ u, const i8* __restrict__ su,
+template <int CH>
+__global__ void __launch_bounds__(512, 1) k_pre2(const u16* __restrict__ g, const u16* __restrict__ u, const i8* __restrict__ su,
                                               int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M,
                                               int K, int ldq) {
     extern __shared__ __align__(16) float buf[];
@@ -52,22 +57,22 @@ __global__ void __launch_bounds__(512) k_pre2(const u16* __restrict__ g, const u
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * K;
     float mx = 0.f;
-    row_walsh16(buf, K,
-              [&](int c, float* v) {
-                  float gv[16], uv[16], sg[16];
-                  load16<TCQ_DT_BF16>(g + base + 16 * c, gv);
-                  load16<TCQ_DT_BF16>(u + base + 16 * c, uv);
-                  load_signs16(su + 16 * c, sg);
+    row_walshc<CH>(buf, K,
+                   [&](int c, float* v) {
+                       float gv[CH], uv[CH], sg[CH];
+                       loadc<TCQ_DT_BF16, CH>(g + base + CH * c, gv);
+                       loadc<TCQ_DT_BF16, CH>(u + base + CH * c, uv);
+                       load_signsc<CH, true>(su + CH * c, sg);
 #pragma unroll
-                  for (int k = 0; k < 16; ++k) v[k] = bf2f(f2bf(gv[k] * uv[k])) * sg[k];
-              },
-              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
-              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+                       for (int k = 0; k < CH; ++k) v[k] = bf2f(f2bf(gv[k] * uv[k])) * sg[k];
+                   },
+                   [&](int i0, const float* v) { store_chunk<CH>(buf, i0, v, mx); },
+                   [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
 }
 
-template <int DT>
-__global__ void __launch_bounds__(512) k_pre_h(const void* __restrict__ x, const i8* __restrict__ su, u16* __restrict__ h,
+template <int DT, int CH>
+__global__ void __launch_bounds__(512, 1) k_pre_h(const void* __restrict__ x, const i8* __restrict__ su, u16* __restrict__ h,
                                                u16* __restrict__ hT, int M, int K, int ldh) {
     extern __shared__ __align__(16) float buf[];
     pdl_launch_dependents();
@@ -75,32 +80,33 @@ __global__ void __launch_bounds__(512) k_pre_h(const void* __restrict__ x, const
     const int tok = blockIdx.x;
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
-    row_walsh16(buf, K,
-              [&](int c, float* v) {
-                  float sg[16];
-                  load16<DT>(xr + (size_t)16 * c * es, v);
-                  load_signs16(su + 16 * c, sg);
+    row_walshc<CH>(buf, K,
+                   [&](int c, float* v) {
+                       float sg[CH];
+                       loadc<DT, CH>(xr + (size_t)CH * c * es, v);
+                       load_signsc<CH, true>(su + CH * c, sg);
 #pragma unroll
-                  for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
-              },
-              [&](int i0, const float* v) {
-                  u32 w[8];
-                  pack_bf16x16(v, w);
-                  if (h) store16_bf16_any(h + (size_t)tok * K + i0, w);
-                  if (hT) {
+                       for (int k = 0; k < CH; ++k) v[k] = v[k] * sg[k];
+                   },
+                   [&](int i0, const float* v) {
+                       u32 w[CH / 2];
+                       pack_bf16c<CH>(v, w);
+                       if (h) store_bf16c_any<CH>(h + (size_t)tok * K + i0, w);
+                       if (hT) {
 #pragma unroll
-                      for (int k = 0; k < 16; ++k) hT[(size_t)(i0 + k) * ldh + tok] = (u16)((k & 1) ? (w[k >> 1] >> 16) : (w[k >> 1] & 0xffffu));
-                  }
-              },
-              [&](int i, float v) {
-                  const u16 b = f2bf(v);
-                  if (h) h[(size_t)tok * K + i] = b;
-                  if (hT) hT[(size_t)i * ldh + tok] = b;
-              });
+                           for (int k = 0; k < CH; ++k)
+                               hT[(size_t)(i0 + k) * ldh + tok] = (u16)((k & 1) ? (w[k >> 1] >> 16) : (w[k >> 1] & 0xffffu));
+                       }
+                   },
+                   [&](int i, float v) {
+                       const u16 b = f2bf(v);
+                       if (h) h[(size_t)tok * K + i] = b;
+                       if (hT) hT[(size_t)i * ldh + tok] = b;
+                   });
 }
 
-template <int DT, int OT>
-__global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, const i8* __restrict__ sg, void* __restrict__ y,
+template <int DT, int OT, int CH>
+__global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, const i8* __restrict__ sg, void* __restrict__ y,
                                                 int M, int D, int inverse) {
     extern __shared__ __align__(16) float buf[];
     pdl_launch_dependents();
@@ -108,74 +114,74 @@ __global__ void __launch_bounds__(512) k_rotate(const void* __restrict__ x, cons
     const int tok = blockIdx.x;
     const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
     const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * D * es;
-    row_walsh16(buf, D,
-              [&](int c, float* v) {
-                  load16<DT>(xr + (size_t)16 * c * es, v);
-                  if (!inverse) {
-                      float s16[16];
-                      load_signs16(sg + 16 * c, s16);
+    row_walshc<CH>(buf, D,
+                   [&](int c, float* v) {
+                       loadc<DT, CH>(xr + (size_t)CH * c * es, v);
+                       if (!inverse) {
+                           float s16[CH];
+                           load_signsc<CH, true>(sg + CH * c, s16);
 #pragma unroll
-                      for (int k = 0; k < 16; ++k) v[k] = v[k] * s16[k];
-                  }
-              },
-              [&](int i0, const float* vin) {
-                  float v[16];
+                           for (int k = 0; k < CH; ++k) v[k] = v[k] * s16[k];
+                       }
+                   },
+                   [&](int i0, const float* vin) {
+                       float v[CH];
 #pragma unroll
-                  for (int k = 0; k < 16; ++k) v[k] = vin[k];
-                  if (inverse) {
-                      float s16[16];
-                      load_signs16(sg + i0, s16);
+                       for (int k = 0; k < CH; ++k) v[k] = vin[k];
+                       if (inverse) {
+                           float s16[CH];
+                           load_signsc<CH, true>(sg + i0, s16);
 #pragma unroll
-                      for (int k = 0; k < 16; ++k) v[k] = v[k] * s16[k];
-                  }
-                  if (OT == TCQ_DT_F32) {
-                      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + (size_t)tok * D + i0);
+                           for (int k = 0; k < CH; ++k) v[k] = v[k] * s16[k];
+                       }
+                       if (OT == TCQ_DT_F32) {
+                           float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + (size_t)tok * D + i0);
 #pragma unroll
-                      for (int q = 0; q < 4; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                  } else {
-                      u32 w[8];
-                      pack_bf16x16(v, w);
-                      store16_bf16(reinterpret_cast<u16*>(y) + (size_t)tok * D + i0, w);
-                  }
-              },
-              [&](int i, float v) {
-                  if (inverse) v = v * (float)sg[i];
-                  if (OT == TCQ_DT_F32) reinterpret_cast<float*>(y)[(size_t)tok * D + i] = v;
-                  else reinterpret_cast<u16*>(y)[(size_t)tok * D + i] = f2bf(v);
-              });
+                           for (int q = 0; q < CH / 4; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                       } else {
+                           u32 w[CH / 2];
+                           pack_bf16c<CH>(v, w);
+                           store_bf16c<CH>(reinterpret_cast<u16*>(y) + (size_t)tok * D + i0, w);
+                       }
+                   },
+                   [&](int i, float v) {
+                       if (inverse) v = v * (float)sg[i];
+                       if (OT == TCQ_DT_F32) reinterpret_cast<float*>(y)[(size_t)tok * D + i] = v;
+                       else reinterpret_cast<u16*>(y)[(size_t)tok * D + i] = f2bf(v);
+                   });
 }
 
 // Epilogue of one layer on one token: SCALE(acc[base + i]) -> block Walsh -> * sv -> + bias -> BF16 (-> act).
-// out(i, b): one BF16 result; out16(i0, w): the 16 results of chunk i0 as 8 packed words (element i0 + k in the low
-// half of w[k / 2] for even k). sv / bias may be shared-memory copies.
-template <int AT, class Out, class Out16>
+// out(i, b): one BF16 result; outc(i0, w): the CH results of chunk i0 as CH / 2 packed words (element i0 + k in the
+// low half of w[k / 2] for even k). sv / bias / rs may be shared-memory copies.
+template <int AT, int CH, class Out, class Outc>
 __device__ __forceinline__ void post_row(float* buf, const void* acc, size_t base, float s, const float* rs, const i8* sv,
-                                         const float* bias, int N, Out out, Out16 out16) {
-    row_walsh16(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, s, rs ? rs + 16 * c : nullptr, v); },
-                [&](int i0, const float* vin) {
-                    float v[16], sg[16];
-                    load_signs16_any(sv + i0, sg);
+                                         const float* bias, int N, Out out, Outc outc) {
+    row_walshc<CH>(buf, N, [&](int c, float* v) { load_scaledc<AT, CH>(acc, base + CH * c, s, rs ? rs + CH * c : nullptr, v); },
+                   [&](int i0, const float* vin) {
+                       float v[CH], sg[CH];
+                       load_signsc<CH, false>(sv + i0, sg);
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) v[k] = vin[k] * sg[k];
-                    if (bias) {
-                        float bb[16];
-                        load_f16x_any(bias + i0, bb);
+                       for (int k = 0; k < CH; ++k) v[k] = vin[k] * sg[k];
+                       if (bias) {
+                           float bb[CH];
+                           load_f32c<CH, false>(bias + i0, bb);
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) v[k] = v[k] + bb[k];
-                    }
-                    u32 w[8];
-                    pack_bf16x16(v, w);
-                    out16(i0, w);
-                },
-                [&](int i, float v) {
-                    v = v * (float)sv[i];
-                    if (bias) v = v + bias[i];
-                    out(i, f2bf(v));
-                });
+                           for (int k = 0; k < CH; ++k) v[k] = v[k] + bb[k];
+                       }
+                       u32 w[CH / 2];
+                       pack_bf16c<CH>(v, w);
+                       outc(i0, w);
+                   },
+                   [&](int i, float v) {
+                       v = v * (float)sv[i];
+                       if (bias) v = v + bias[i];
+                       out(i, f2bf(v));
+                   });
 }
 
-template <int AT>
-__global__ void __launch_bounds__(512) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+template <int AT, int CH>
+__global__ void __launch_bounds__(512, 1) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, u16* __restrict__ y, int M,
                                               int N, int lda, int col0, int stage) {
     extern __shared__ __align__(16) float buf[];
@@ -188,14 +194,14 @@ __global__ void __launch_bounds__(512) k_post(const void* __restrict__ acc, cons
     pdl_wait();
     const int tok = blockIdx.x;
     u16* yo = y + (size_t)tok * N;
-    post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 b) { yo[i] = b; },
-                 [&](int i0, const u32* w) { store16_bf16_any(yo + i0, w); });
+    post_row<AT, CH>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 b) { yo[i] = b; },
+                     [&](int i0, const u32* w) { store_bf16c_any<CH>(yo + i0, w); });
 }
 
 // Several layers sharing the accumulator row. grid.y == 1: the layers one after another in one block (post3);
 // grid.y == number of layers: one block per (token, layer) (postg). act0: activation table on layer 0's output.
-template <int AT>
-__global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc, const float* __restrict__ s,
+template <int AT, int CH>
+__global__ void __launch_bounds__(512, 1) k_post_multi(const void* __restrict__ acc, const float* __restrict__ s,
                                                     const float* __restrict__ rs, const i8* __restrict__ sv,
                                                     const float* __restrict__ bias, const u16* __restrict__ lut, u16* y0, u16* y1,
                                                     u16* y2, int M, int n0, int n1, int n2, int lda, int act0, int nmax,
@@ -220,18 +226,18 @@ __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc
         const int c0 = seg == 0 ? 0 : seg == 1 ? n0 : n0 + n1;
         u16* yo = (seg == 0 ? y0 : seg == 1 ? y1 : y2) + (size_t)tok * N;
         const bool act = act0 && seg == 0;
-        post_row<AT>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rsc ? rsc + (c0 - cs) : nullptr, svc + (c0 - cs),
-                     biasc ? biasc + (c0 - cs) : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; },
-                     [&](int i0, const u32* w) {
-                         if (act) {
-                             u32 a[8];
+        post_row<AT, CH>(buf, acc, (size_t)tok * lda + c0, s ? s[tok] : 1.f, rsc ? rsc + (c0 - cs) : nullptr, svc + (c0 - cs),
+                         biasc ? biasc + (c0 - cs) : nullptr, N, [&](int i, u16 b) { yo[i] = act ? lut[b] : b; },
+                         [&](int i0, const u32* w) {
+                             if (act) {
+                                 u32 a[CH / 2];
 #pragma unroll
-                             for (int k = 0; k < 8; ++k) a[k] = (u32)lut[w[k] & 0xffffu] | ((u32)lut[w[k] >> 16] << 16);
-                             store16_bf16_any(yo + i0, a);
-                         } else {
-                             store16_bf16_any(yo + i0, w);
-                         }
-                     });
+                                 for (int k = 0; k < CH / 2; ++k) a[k] = (u32)lut[w[k] & 0xffffu] | ((u32)lut[w[k] >> 16] << 16);
+                                 store_bf16c_any<CH>(yo + i0, a);
+                             } else {
+                                 store_bf16c_any<CH>(yo + i0, w);
+                             }
+                         });
     }
 }
 
@@ -240,12 +246,13 @@ __global__ void __launch_bounds__(512) k_post_multi(const void* __restrict__ acc
 //   y = post(acc)        as k_post: SCALE(acc) -> block Walsh -> * sv -> + bias -> BF16          (acc != NULL)
 //       or y = yg        a BF16 tensor                                                            (yg != NULL)
 //   h = BF16(x + y)      written to hout (h = x when there is no y)
-//   n = norm(h)          norm_chunks with norm_threads(N) threads: the same arithmetic, thread count and sum order as
-//                        tcq_add_norm; BF16(n) written to nout when given
+//   n = norm(h)          norm_chunks: the same arithmetic and sum order as tcq_add_norm; BF16(n) written to nout
+//                        when given
 //   q / q4, scale        = pre(BF16(n), su) as k_pre on a BF16 input                             (su != NULL)
-// Each step is bit-identical to the separate kernel. Shared memory: N floats (Walsh buffer) + N BF16 (y, then n).
-template <int AT, int KIND, bool WBF16, int NC>
-__global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+// Each step is bit-identical to the separate kernel. Shared memory: N floats (Walsh buffer) + N BF16 (y, then n),
+// then the staged constants and the copy area of the row inputs.
+template <int AT, int KIND, bool WBF16, int NC, int CH>
+__global__ void __launch_bounds__(512, 1) k_chain(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                                const i8* __restrict__ sv, const float* __restrict__ bias, int lda, int col0,
                                                const u16* __restrict__ yg, const u16* __restrict__ x, u16* __restrict__ hout,
                                                u16* __restrict__ nout, const void* __restrict__ w, const void* __restrict__ b,
@@ -267,11 +274,12 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
     const i8* suc = static_cast<const i8*>(stage_const(sp, su, N, on));
     __syncthreads();
     pdl_wait();
-    const int tok = blockIdx.x, nch = N >> 4;
+    const int tok = blockIdx.x, nch = N / CH;
     const size_t base = (size_t)tok * N;
     // With staging on, the thread's first chunk of x (and of y / the modulation) is copied into shared memory
     // asynchronously now, with the accumulator loads in flight, so that the residual add and the norm find it there
     // (the copy area follows the constants: x, then y when added from a tensor, then the two modulation vectors).
+    // Chunks of CH = 4 are 8 bytes: two threads' chunks form one 16-byte copy, issued by the even thread.
     const bool first = (int)threadIdx.x < nch;
     const u16* ms = mscale ? mscale + (size_t)(tok / mod_rows) * ld_mod : nullptr;
     const u16* mh = mscale ? mshift + (size_t)(tok / mod_rows) * ld_mod : nullptr;
@@ -280,77 +288,83 @@ __global__ void __launch_bounds__(512) k_chain(const void* __restrict__ acc, con
     u16* ys = xs + N;
     u16* mss = ys + (ycopy ? N : 0);
     u16* mhs = mss + N;
-    if (on && first) {
-        const int o = 16 * threadIdx.x;
-        cp_async16(xs + o, x + base + o);
-        cp_async16(xs + o + 8, x + base + o + 8);
-        if (ycopy) {
-            cp_async16(ys + o, yg + base + o);
-            cp_async16(ys + o + 8, yg + base + o + 8);
-        }
-        if (mcopy) {
-            cp_async16(mss + o, ms + o);
-            cp_async16(mss + o + 8, ms + o + 8);
-            cp_async16(mhs + o, mh + o);
-            cp_async16(mhs + o + 8, mh + o + 8);
-        }
-    }
-    if (acc)                                        // ends with a block barrier: yb complete
-        post_row<AT>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 v) { yb[i] = v; },
-                     [&](int i0, const u32* w) { store16_bf16(yb + i0, w); });
-    ModChunk m0{};
     if (on) {
-        cp_async_wait_all();                        // this thread's copies (it reads only its own chunk)
-        if (mcopy && first) load_mod_chunk_smem(m0, mss + 16 * threadIdx.x, mhs + 16 * threadIdx.x);
-    }
-    float v[NC][16];
-#pragma unroll
-    for (int k = 0; k < NC; ++k) {
-        const int c = threadIdx.x + k * blockDim.x;
-        if (c < nch) {
-            if (k == 0 && on) load_bf16x16_any(xs + 16 * c, v[k]);
-            else load_bf16x16(x + base + 16 * c, v[k]);
-            if (acc || yg) {
-                float t[16];
-                if (acc) load_bf16x16_any(yb + 16 * c, t);
-                else if (k == 0 && on) load_bf16x16_any(ys + 16 * c, t);
-                else load_bf16x16(yg + base + 16 * c, t);
-                add_round_chunk(v[k], t, hout ? hout + base + 16 * c : nullptr);
+        for (int o = 8 * threadIdx.x; o < (nch < (int)blockDim.x ? nch : (int)blockDim.x) * CH; o += 8 * blockDim.x) {
+            cp_async16(xs + o, x + base + o);
+            if (ycopy) cp_async16(ys + o, yg + base + o);
+            if (mcopy) {
+                cp_async16(mss + o, ms + o);
+                cp_async16(mhs + o, mh + o);
             }
         }
     }
-    norm_chunks<KIND, WBF16, NC>(v, N, wc, bc, ms, mh, eps, red, m0);   // synchronizes: every thread is past its reads of yb
+    if (acc)                                        // ends with a block barrier: yb complete
+        post_row<AT, CH>(buf, acc, (size_t)tok * lda + col0, s ? s[tok] : 1.f, rsc, svc, biasc, N, [&](int i, u16 v) { yb[i] = v; },
+                         [&](int i0, const u32* ww) { store_bf16c<CH>(yb + i0, ww); });
+    ModChunk<CH> m0{};
+    if (on) {
+        cp_async_wait_all();
+        __syncthreads();                            // copies of 16 bytes span the chunks of two threads
+        if (mcopy && first) load_mod_chunk<CH, false>(m0, mss + CH * threadIdx.x, mhs + CH * threadIdx.x);
+    }
+    float v[NC][CH];
 #pragma unroll
     for (int k = 0; k < NC; ++k) {
         const int c = threadIdx.x + k * blockDim.x;
         if (c < nch) {
-            u32 wn[8];
-            pack_bf16x16(v[k], wn);
-            if (nout) store16_bf16(nout + base + 16 * c, wn);
-            store16_bf16(yb + 16 * c, wn);
+            if (k == 0 && on) load_bf16c_any<CH>(xs + CH * c, v[k]);
+            else loadc<TCQ_DT_BF16, CH>(x + base + CH * c, v[k]);
+            if (acc || yg) {
+                float t[CH];
+                if (acc) load_bf16c_any<CH>(yb + CH * c, t);
+                else if (k == 0 && on) load_bf16c_any<CH>(ys + CH * c, t);
+                else loadc<TCQ_DT_BF16, CH>(yg + base + CH * c, t);
+                add_round_chunk<CH>(v[k], t, hout ? hout + base + CH * c : nullptr);
+            }
+        }
+    }
+    norm_chunks<KIND, WBF16, NC, CH>(v, N, wc, bc, ms, mh, eps, red, m0);   // synchronizes: all reads of yb are done
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < nch) {
+            u32 wn[CH / 2];
+            pack_bf16c<CH>(v[k], wn);
+            if (nout) store_bf16c<CH>(nout + base + CH * c, wn);
+            store_bf16c<CH>(yb + CH * c, wn);
         }
     }
     if (!su) return;
     __syncthreads();
     float mx = 0.f;
-    row_walsh16(buf, N,
-              [&](int c, float* vv) {
-                  float sg[16];
-                  load_signs16_any(suc + 16 * c, sg);
-                  float nb[16];
-                  load_bf16x16_any(yb + 16 * c, nb);
+    row_walshc<CH>(buf, N,
+                   [&](int c, float* vv) {
+                       float sg[CH], nb[CH];
+                       load_signsc<CH, false>(suc + CH * c, sg);
+                       load_bf16c_any<CH>(yb + CH * c, nb);
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) vv[i] = nb[i] * sg[i];
-              },
-              [&](int i0, const float* vv) { store_chunk(buf, i0, vv, mx); },
-              [&](int i, float val) { buf[swz(i)] = val; mx = fmaxf(mx, fabsf(val)); });
+                       for (int i = 0; i < CH; ++i) vv[i] = nb[i] * sg[i];
+                   },
+                   [&](int i0, const float* vv) { store_chunk<CH>(buf, i0, vv, mx); },
+                   [&](int i, float val) { buf[swz(i)] = val; mx = fmaxf(mx, fabsf(val)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
+// The finished row in buf as the next transform's input chunk c.
+template <int CH>
+__device__ __forceinline__ void buf_chunk(const float* buf, int c, float* v) {
+    const float4* b4 = reinterpret_cast<const float4*>(buf);
+#pragma unroll
+    for (int g = 0; g < CH / 4; ++g) {
+        const float4 a = b4[swz(CH * c + 4 * g) >> 2];
+        v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
+    }
 }
 
 // Gated-MLP middle (kernels.py:263-278): g = lut(BF16(post(gate))), u = BF16(post(up)), x = BF16(g * u) * su,
 // block Walsh, INT8. Shared memory: N floats + N BF16.
-template <int AT>
-__global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+template <int AT, int CH>
+__global__ void __launch_bounds__(512, 1) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const u16* __restrict__ lut, const i8* __restrict__ su,
                                               int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M, int N,
                                               int lda, int ldq, int stage) {
@@ -368,31 +382,23 @@ __global__ void __launch_bounds__(512) k_mid2(const void* __restrict__ acc, cons
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * lda;
     const float st = s ? s[tok] : 1.f;
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
-              [&](int i, float v) { gb[i] = lut[f2bf(v * (float)svc[i])]; });
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + N + 16 * c, st, rsc ? rsc + N + 16 * c : nullptr, v); },
-                [&](int i, float v) {
-                    const u16 u = f2bf(v * (float)svc[N + i]);
-                    buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)suc[i];
-                });
+    row_walsh<CH>(buf, N, [&](int c, float* v) { load_scaledc<AT, CH>(acc, base + CH * c, st, rsc ? rsc + CH * c : nullptr, v); },
+                  [&](int i, float v) { gb[i] = lut[f2bf(v * (float)svc[i])]; });
+    row_walsh<CH>(buf, N, [&](int c, float* v) { load_scaledc<AT, CH>(acc, base + N + CH * c, st, rsc ? rsc + N + CH * c : nullptr, v); },
+                  [&](int i, float v) {
+                      const u16 u = f2bf(v * (float)svc[N + i]);
+                      buf[swz(i)] = bf2f(f2bf(bf2f(gb[i]) * bf2f(u))) * (float)suc[i];
+                  });
     float mx = 0.f;
-    row_walsh16(buf, N,
-              [&](int c, float* v) {
-                  const float4* b4 = reinterpret_cast<const float4*>(buf);
-#pragma unroll
-                  for (int g = 0; g < 4; ++g) {
-                      const float4 a = b4[swz(16 * c + 4 * g) >> 2];
-                      v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
-                  }
-              },
-              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
-              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    row_walshc<CH>(buf, N, [&](int c, float* v) { buf_chunk<CH>(buf, c, v); },
+                   [&](int i0, const float* v) { store_chunk<CH>(buf, i0, v, mx); },
+                   [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
 // Plain-MLP middle (kernels.py:280-292): x = lut(BF16(post(acc) + bias)) * su, block Walsh, INT8.
-template <int AT>
-__global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+template <int AT, int CH>
+__global__ void __launch_bounds__(512, 1) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, const u16* __restrict__ lut,
                                               const i8* __restrict__ su, int8_t* __restrict__ q, int* __restrict__ q4,
                                               float* __restrict__ scale, int M, int N, int lda, int ldq, int stage) {
@@ -410,24 +416,16 @@ __global__ void __launch_bounds__(512) k_mid1(const void* __restrict__ acc, cons
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * lda;
     const float st = s ? s[tok] : 1.f;
-    row_walsh(buf, N, [&](int c, float* v) { load_scaled16<AT>(acc, base + 16 * c, st, rsc ? rsc + 16 * c : nullptr, v); },
-                [&](int i, float v) {
-                    v = v * (float)svc[i];
-                    if (biasc) v = v + biasc[i];
-                    buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)suc[i];
-                });
+    row_walsh<CH>(buf, N, [&](int c, float* v) { load_scaledc<AT, CH>(acc, base + CH * c, st, rsc ? rsc + CH * c : nullptr, v); },
+                  [&](int i, float v) {
+                      v = v * (float)svc[i];
+                      if (biasc) v = v + biasc[i];
+                      buf[swz(i)] = bf2f(lut[f2bf(v)]) * (float)suc[i];
+                  });
     float mx = 0.f;
-    row_walsh16(buf, N,
-              [&](int c, float* v) {
-                  const float4* b4 = reinterpret_cast<const float4*>(buf);
-#pragma unroll
-                  for (int g = 0; g < 4; ++g) {
-                      const float4 a = b4[swz(16 * c + 4 * g) >> 2];
-                      v[4 * g] = a.x; v[4 * g + 1] = a.y; v[4 * g + 2] = a.z; v[4 * g + 3] = a.w;
-                  }
-              },
-              [&](int i0, const float* v) { store_chunk(buf, i0, v, mx); },
-              [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    row_walshc<CH>(buf, N, [&](int c, float* v) { buf_chunk<CH>(buf, c, v); },
+                   [&](int i0, const float* v) { store_chunk<CH>(buf, i0, v, mx); },
+                   [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
@@ -447,7 +445,7 @@ __global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_
     float mx = 0.f;
     for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
         float v[16];
-        load16<DT>(xr + (size_t)16 * c * es, v);
+        loadc<DT, 16>(xr + (size_t)16 * c * es, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(v[k]));
     }
@@ -456,7 +454,7 @@ __global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_
     if (threadIdx.x == 0) scale[tok] = s;
     for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
         float v[16];
-        load16<DT>(xr + (size_t)16 * c * es, v);
+        loadc<DT, 16>(xr + (size_t)16 * c * es, v);
         u32 w[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g)
@@ -467,11 +465,26 @@ __global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_
 }
 
 // ---------------------------------------------------------------------------------------------------- host side
-int threads_for(int K) {
-    int t = ((K >> 4) + 31) & ~31;
+int threads_for(int K, int CH) {
+    int t = ((K / CH) + 31) & ~31;
     if (t < 32) t = 32;
     if (t > 512) t = 512;
     return t;
+}
+
+// Elements per thread chunk of a launch of M rows of width K: 4 while the launch's threads at that chunking fit on the
+// machine at once (at most `per_sm` threads per SM; each thread's instruction latency bounds such a launch, so more
+// threads per row finish it sooner), 16 otherwise (more rows: throughput, fewer threads per row).
+int rows_ch(int M, int K, int per_sm) {
+    return (long long)M * threads_for(K, 4) <= (long long)tcq_sm_count() * per_sm ? 4 : 16;
+}
+constexpr int kLightPerSm = 1024;   // row kernels of few registers (pre, rotate)
+constexpr int kHeavyPerSm = 512;    // row kernels with the epilogue's operands in registers (post, middles, chain)
+
+// f(std::integral_constant<int, CH>{}) for the chunk width ch (4 or 16).
+template <class F>
+int with_ch(int ch, F f) {
+    return ch == 4 ? f(std::integral_constant<int, 4>{}) : f(std::integral_constant<int, 16>{});
 }
 
 bool width_ok(int K) { return K > 0 && (K & 15) == 0 && K <= kMaxWidth; }
@@ -542,13 +555,16 @@ int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16))) return TCQ_ERR_ALIGN;
     const size_t smem = (size_t)4 * K;
-    const int T = threads_for(K);
-    switch (x_dtype) {
-        case TCQ_DT_BF16: return launch(k_pre<TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
-        case TCQ_DT_F16: return launch(k_pre<TCQ_DT_F16>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
-        case TCQ_DT_F32: return launch(k_pre<TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, K, kLightPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(K, CH);
+        switch (x_dtype) {
+            case TCQ_DT_BF16: return launch(k_pre<TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+            case TCQ_DT_F16: return launch(k_pre<TCQ_DT_F16, CH>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+            case TCQ_DT_F32: return launch(k_pre<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, x, (const i8*)su, q, (int*)q4, scale, M, K, ldq);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_pre2(const uint16_t* g, const uint16_t* u, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int M, int K,
@@ -557,8 +573,11 @@ int tcq_pre2(const uint16_t* g, const uint16_t* u, const int8_t* su, int8_t* q, 
     if (M <= 0 || !width_ok(K)) return TCQ_ERR_SHAPE;
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!tcq_aligned(g, 16) || !tcq_aligned(u, 16) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16))) return TCQ_ERR_ALIGN;
-    return launch(k_pre2, dim3(M), threads_for(K), (size_t)4 * K, stream, (const u16*)g, (const u16*)u, (const i8*)su, q,
-                  (int*)q4, scale, M, K, ldq);
+    return with_ch(rows_ch(M, K, kLightPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        return launch(k_pre2<CH>, dim3(M), threads_for(K, CH), (size_t)4 * K, stream, (const u16*)g, (const u16*)u, (const i8*)su,
+                      q, (int*)q4, scale, M, K, ldq);
+    });
 }
 
 int tcq_pre_h(const void* x, int x_dtype, const int8_t* su, uint16_t* h, uint16_t* hT, int M, int K, int ldh, void* stream) {
@@ -567,13 +586,16 @@ int tcq_pre_h(const void* x, int x_dtype, const int8_t* su, uint16_t* h, uint16_
     if (hT && ldh < M) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || !tcq_aligned(su, 16)) return TCQ_ERR_ALIGN;
     const size_t smem = (size_t)4 * K;
-    const int T = threads_for(K);
-    switch (x_dtype) {
-        case TCQ_DT_BF16: return launch(k_pre_h<TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
-        case TCQ_DT_F16: return launch(k_pre_h<TCQ_DT_F16>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
-        case TCQ_DT_F32: return launch(k_pre_h<TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, K, kLightPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(K, CH);
+        switch (x_dtype) {
+            case TCQ_DT_BF16: return launch(k_pre_h<TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+            case TCQ_DT_F16: return launch(k_pre_h<TCQ_DT_F16, CH>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+            case TCQ_DT_F32: return launch(k_pre_h<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, x, (const i8*)su, (u16*)h, (u16*)hT, M, K, ldh);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_rotate(const void* x, int x_dtype, const int8_t* signs, void* y, int y_dtype, int M, int D, int inverse,
@@ -582,22 +604,26 @@ int tcq_rotate(const void* x, int x_dtype, const int8_t* signs, void* y, int y_d
     if (M <= 0 || !width_ok(D)) return TCQ_ERR_SHAPE;
     if (!tcq_aligned(x, 16) || !tcq_aligned(signs, 16)) return TCQ_ERR_ALIGN;
     const size_t smem = (size_t)4 * D;
-    const int T = threads_for(D);
     const int inv = inverse ? 1 : 0;
     if (y_dtype != TCQ_DT_F32 && y_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
+    if (!tcq_aligned(y, 16)) return TCQ_ERR_ALIGN;
     const bool of = y_dtype == TCQ_DT_F32;
-    switch (x_dtype) {
-        case TCQ_DT_BF16:
-            return of ? launch(k_rotate<TCQ_DT_BF16, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
-                      : launch(k_rotate<TCQ_DT_BF16, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
-        case TCQ_DT_F16:
-            return of ? launch(k_rotate<TCQ_DT_F16, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
-                      : launch(k_rotate<TCQ_DT_F16, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
-        case TCQ_DT_F32:
-            return of ? launch(k_rotate<TCQ_DT_F32, TCQ_DT_F32>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
-                      : launch(k_rotate<TCQ_DT_F32, TCQ_DT_BF16>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, D, kLightPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(D, CH);
+        switch (x_dtype) {
+            case TCQ_DT_BF16:
+                return of ? launch(k_rotate<TCQ_DT_BF16, TCQ_DT_F32, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                          : launch(k_rotate<TCQ_DT_BF16, TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+            case TCQ_DT_F16:
+                return of ? launch(k_rotate<TCQ_DT_F16, TCQ_DT_F32, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                          : launch(k_rotate<TCQ_DT_F16, TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+            case TCQ_DT_F32:
+                return of ? launch(k_rotate<TCQ_DT_F32, TCQ_DT_F32, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv)
+                          : launch(k_rotate<TCQ_DT_F32, TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, x, (const i8*)signs, y, M, D, inv);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
@@ -611,13 +637,16 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
-    const int T = threads_for(N);
-    switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
-        case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
-        case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(N, CH);
+        switch (acc_dtype) {
+            case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
+            case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
+            case TCQ_DT_BF16: return launch(k_post<TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias, int lda,
@@ -640,7 +669,9 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
     if (!tcq_aligned(x, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)) || (n && !tcq_aligned(n, 16)) ||
         (su && !tcq_aligned(su, 16)) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
-    const int T = norm_threads(N);
+    // Chunks of 4 for a few rows up to 2048 wide (the norm's sum order does not depend on the chunking), else 16.
+    const bool c4 = N <= 2048 && rows_ch(M, N, kHeavyPerSm) == 4;
+    const int T = norm_threads(N, c4 ? 4 : 16);
     const bool wb = wb_dtype == TCQ_DT_BF16, i32 = acc && acc_dtype == TCQ_DT_I32;
     // Layer constants staged by the kernel (the same set, in bytes): rs (I32 accumulators), bias, sv, w, b, su.
     const size_t cb = (acc ? (size_t)(i32 ? 4 * N : 0) + (bias ? 4 * N : 0) + N : 0) + (size_t)(w ? 1 : 0) * (wb ? 2 : 4) * N +
@@ -649,9 +680,9 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
     const size_t pb = (size_t)2 * N * (1 + (!acc && y ? 1 : 0) + (mod_scale ? 2 : 0));
     const int stage = tcq_stage_rows(M, cb, kStageMaxBytes) && (size_t)6 * N + cb + pb <= (size_t)kStageMaxSmem;
     const size_t smem = (size_t)6 * N + (stage ? cb + pb : 0);
-    // One 16-element chunk per thread up to N = 8192 (T = N / 16 threads); wider rows hold kNormMaxChunks per thread.
-    const bool one = (N >> 4) <= 512;
-#define TCQ_CHAIN(AT_, K_, WB_) (one ? k_chain<AT_, K_, WB_, 1> : k_chain<AT_, K_, WB_, kNormMaxChunks>)
+    auto pick = [&](auto k0, auto k1, auto k2) { return c4 ? k0 : N <= 8192 ? k1 : k2; };
+#define TCQ_CHAIN(AT_, K_, WB_) \
+    pick(k_chain<AT_, K_, WB_, 1, 4>, k_chain<AT_, K_, WB_, 1, 16>, k_chain<AT_, K_, WB_, kNormMaxChunks, 16>)
     auto kern = kind == 0 ? (i32 ? (wb ? TCQ_CHAIN(TCQ_DT_I32, 0, true) : TCQ_CHAIN(TCQ_DT_I32, 0, false))
                                  : (wb ? TCQ_CHAIN(TCQ_DT_F32, 0, true) : TCQ_CHAIN(TCQ_DT_F32, 0, false)))
                           : (i32 ? (wb ? TCQ_CHAIN(TCQ_DT_I32, 1, true) : TCQ_CHAIN(TCQ_DT_I32, 1, false))
@@ -682,13 +713,16 @@ static int post_multi(const void* acc, int acc_dtype, const float* s, const floa
     const size_t cb = ntot * ((acc_dtype != TCQ_DT_F32 && rs ? 4 : 0) + (bias ? 4 : 0) + 1);
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)4 * nmax + (st ? cb : 0);
-    const int T = threads_for(nmax);
-    switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
-        case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
-        case TCQ_DT_BF16: return launch(k_post_multi<TCQ_DT_BF16>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M * (int)grid.y, nmax, kHeavyPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(nmax, CH);
+        switch (acc_dtype) {
+            case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32, CH>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
+            case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32, CH>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
+            case TCQ_DT_BF16: return launch(k_post_multi<TCQ_DT_BF16, CH>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_post3(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
@@ -715,13 +749,16 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 8 * N : 0) + 2 * N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)6 * N + (st ? cb : 0);
-    const int T = threads_for(N);
-    switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        case TCQ_DT_BF16: return launch(k_mid2<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(N, CH);
+        switch (acc_dtype) {
+            case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            case TCQ_DT_BF16: return launch(k_mid2<TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias,
@@ -738,13 +775,16 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
-    const int T = threads_for(N);
-    switch (acc_dtype) {
-        case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        case TCQ_DT_BF16: return launch(k_mid1<TCQ_DT_BF16>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
-        default: return TCQ_ERR_DTYPE;
-    }
+    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+        constexpr int CH = decltype(C)::value;
+        const int T = threads_for(N, CH);
+        switch (acc_dtype) {
+            case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            case TCQ_DT_BF16: return launch(k_mid1<TCQ_DT_BF16, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
+            default: return (int)TCQ_ERR_DTYPE;
+        }
+    });
 }
 
 }  // extern "C"

@@ -5,6 +5,11 @@
 // (tcq_format.py:26-30); each block gets the FP32 Walsh transform with stages h = 1, 2, 4, ... and the scale
 // (float)(1 / sqrt(w)) (tcq_format.py:44-55); every kernel that includes this header computes it the same way, so
 // their results agree bit for bit.
+//
+// A thread holds CH contiguous elements of the row (a chunk; CH = 4 or 16). CH = 16 gives every thread more
+// independent work (many-row launches, bound by throughput); CH = 4 puts four times as many threads on a row, so a
+// launch of a few rows (bound by the latency of each thread's instruction stream) finishes sooner. The arithmetic is
+// the same for both: only which thread performs an addition changes, never its operands or their order.
 #pragma once
 #include "tcq_common.cuh"
 
@@ -32,61 +37,66 @@ __device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bo
     }
 }
 
-// ld16(c, v): the 16 inputs of chunk c (indices 16c .. 16c+15). fin(i, value): called exactly once per index with the
-// finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]). fin16(i0, v): the
-// same for the 16 finished values of a whole chunk i0 .. i0+15 at once (blocks of up to 512, finished in registers),
-// so that callers can load their per-index operands and store their results 16 bytes at a time.
-// Ends with a __syncthreads() so that values fin / fin16 stored to buf are visible to the whole block.
+template <int CH>
+struct ChunkLog {
+    static constexpr int value = CH == 16 ? 4 : 2;
+};
+
+// ldc(c, v): the CH inputs of chunk c (indices CH c .. CH c + CH - 1). fin(i, value): called exactly once per index
+// with the finished, scaled value (by the thread that owns index i in that pass; it may write buf[swz(i)]).
+// finc(i0, v): the same for the CH finished values of a whole chunk i0 .. i0 + CH - 1 at once (blocks of up to
+// 32 CH, finished in registers), so that callers load their per-index operands and store their results in vectors.
+// Ends with a __syncthreads() so that values fin / finc stored to buf are visible to the whole block.
 //
-// Stages h = 1..8 run in registers on a thread's 16 contiguous inputs; h = 16..256 across the 32 lanes of a warp,
-// which hold 32 consecutive chunks (lane partner = lane ^ h/16: the lower lane keeps a + b, the upper b' = a - b, the
-// reference's operands in its order; both as one rounding of (+-1) * own + partner); blocks of up to 512 are then
-// done. Wider blocks finish with radix-16 passes through shared memory at stride 512 (and 8192). Threads per row are
-// a multiple of 32, so a warp's chunks are consecutive; blocks are aligned to their width, so a stage never pairs
-// chunks of different blocks. The cross-lane stages are a rolled loop: row kernels run once per launch and are bound
-// by instruction fetch, not by the loop overhead.
-template <class Ld16, class Fin16, class Fin>
-__device__ __forceinline__ void row_walsh16(float* buf, int K, Ld16 ld16, Fin16 fin16, Fin fin) {
-    const int nch = K >> 4, lane = threadIdx.x & 31;
+// Stages h = 1 .. CH/2 run in registers on a thread's CH contiguous inputs; h = CH .. 16 CH across the 32 lanes of a
+// warp, which hold 32 consecutive chunks (lane partner = lane ^ h/CH: the lower lane keeps a + b, the upper
+// b' = a - b, the reference's operands in its order; both as one rounding of (+-1) * own + partner); blocks of up to
+// 32 CH are then done. Wider blocks finish with radix-16 passes through shared memory at stride 32 CH (then 16 times
+// that). Threads per row are a multiple of 32, so a warp's chunks are consecutive; blocks are aligned to their width,
+// so a stage never pairs chunks of different blocks. The cross-lane stages are a rolled loop (less code to fetch).
+template <int CH, class Ldc, class Finc, class Fin>
+__device__ __forceinline__ void row_walshc(float* buf, int K, Ldc ldc, Finc finc, Fin fin) {
+    constexpr int LC = ChunkLog<CH>::value;
+    const int nch = K >> LC, lane = threadIdx.x & 31;
     for (int c0 = threadIdx.x - lane; c0 < nch; c0 += blockDim.x) {        // warp-uniform
         const int c = c0 + lane;
-        float v[16];
+        float v[CH];
         int w = 0;                                                             // width of this chunk's block
         if (c < nch) {
-            ld16(c, v);
-            bfly<4>(v);
-            w = block_of(c << 4, K);
+            ldc(c, v);
+            bfly<LC>(v);
+            w = block_of(c << LC, K);
         } else {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.f;
+            for (int k = 0; k < CH; ++k) v[k] = 0.f;
         }
 #pragma unroll 1
-        for (int hc = 1; hc < 32; hc <<= 1) {                                 // stage h = 16 hc
-            if (!__any_sync(0xffffffffu, w > 16 * hc)) break;
-            const bool act = w > 16 * hc;
+        for (int hc = 1; hc < 32; hc <<= 1) {                                 // stage h = CH hc
+            if (!__any_sync(0xffffffffu, w > CH * hc)) break;
+            const bool act = w > CH * hc;
             const float sg = (lane & hc) ? -1.f : 1.f;                         // upper lane: partner - own
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
+            for (int k = 0; k < CH; ++k) {
                 const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
                 if (act) v[k] = __fmaf_rn(sg, v[k], p);
             }
         }
         if (c < nch) {
-            const int i0 = c << 4;
-            if (w <= 512) {
+            const int i0 = c << LC;
+            if (w <= 32 * CH) {
                 const float sc = wscale(w);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] = v[k] * sc;
-                fin16(i0, v);
+                for (int k = 0; k < CH; ++k) v[k] = v[k] * sc;
+                finc(i0, v);
             } else {
                 float4* b4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                for (int q = 0; q < CH / 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
         }
     }
     __syncthreads();
-    for (int S = 512;; S <<= 4) {
+    for (int S = 32 * CH;; S <<= 4) {
         bool work = false;
         int off = 0;
         for (int rem = K; rem;) {
@@ -110,19 +120,21 @@ __device__ __forceinline__ void row_walsh16(float* buf, int K, Ld16 ld16, Fin16 
     }
 }
 
-template <class Ld16, class Fin>
-__device__ __forceinline__ void row_walsh(float* buf, int K, Ld16 ld16, Fin fin) {
-    row_walsh16(buf, K, ld16, [&](int i0, const float* v) {
+// The transform with a per-index finisher only.
+template <int CH, class Ldc, class Fin>
+__device__ __forceinline__ void row_walsh(float* buf, int K, Ldc ldc, Fin fin) {
+    row_walshc<CH>(buf, K, ldc, [&](int i0, const float* v) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) fin(i0 + k, v[k]);
+        for (int k = 0; k < CH; ++k) fin(i0 + k, v[k]);
     }, fin);
 }
 
-// fin16 of a pass whose result is the finished row in buf (at swz(i)) plus its absolute maximum: four 16-byte stores.
+// finc of a pass whose result is the finished row in buf (at swz(i)) plus its absolute maximum.
+template <int CH>
 __device__ __forceinline__ void store_chunk(float* buf, int i0, const float* v, float& mx) {
     float4* b4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < CH / 4; ++q) {
         b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 #pragma unroll
         for (int k = 0; k < 4; ++k) mx = fmaxf(mx, fabsf(v[4 * q + k]));
@@ -148,75 +160,94 @@ __device__ __forceinline__ int q8(float v, float s) {
     return (int)r;
 }
 
+// One q4 word (four values) per thread and step, so that every thread of the block takes part.
 __device__ __forceinline__ void quantize_store(const float* buf, float mx, float* red, int8_t* q, int* q4, float* scale,
                                                int tok, int K, int ldq) {
     mx = block_max(mx, red);
     const float s = mx > 0.f ? mx / 127.f : 1.f;
     if (threadIdx.x == 0) scale[tok] = s;
-    // Four values (one q4 word) per step, in a rolled loop: the division's code is fetched once, not sixteen times.
     const float4* b4 = reinterpret_cast<const float4*>(buf);
-    for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
-#pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
-            const float4 v = b4[swz(16 * c + 4 * g) >> 2];
-            const u32 w = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
-                          ((u32)(q8(v.w, s) & 0xff) << 24);
-            if (q) reinterpret_cast<u32*>(q + (size_t)tok * K + 16 * c)[g] = w;
-            if (q4) q4[(size_t)(4 * c + g) * ldq + tok] = (int)w;
-        }
+    for (int g = threadIdx.x; g < (K >> 2); g += blockDim.x) {
+        const float4 v = b4[swz(4 * g) >> 2];
+        const u32 w = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
+                      ((u32)(q8(v.w, s) & 0xff) << 24);
+        if (q) reinterpret_cast<u32*>(q + (size_t)tok * K)[g] = w;
+        if (q4) q4[(size_t)g * ldq + tok] = (int)w;
     }
 }
 
 // ---------------------------------------------------------------------------------------------------- chunk I/O
-// The same for a destination of unknown alignment (a caller's output view): 16-byte stores when p allows them.
-__device__ __forceinline__ void store16_bf16_any(u16* p, const u32* w) {
-    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+template <int CH>
+__device__ __forceinline__ void pack_bf16c(const float* v, u32* w) {
+#pragma unroll
+    for (int k = 0; k < CH / 2; ++k) w[k] = f2bf2(v[2 * k], v[2 * k + 1]);
+}
+
+// CH packed BF16 values (2 CH bytes) to p, aligned to 2 CH bytes (global or shared): vector stores.
+template <int CH>
+__device__ __forceinline__ void store_bf16c(u16* p, const u32* w) {
+    if (CH == 16) {
         store16_bf16(p, w);
     } else {
+        *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+    }
+}
+
+// The same for a destination of unknown alignment (a caller's output view): vector stores when p allows them.
+template <int CH>
+__device__ __forceinline__ void store_bf16c_any(u16* p, const u32* w) {
+    if ((reinterpret_cast<uintptr_t>(p) & (2 * CH - 1)) == 0) {
+        store_bf16c<CH>(p, w);
+    } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < CH / 2; ++k) {
             p[2 * k] = (u16)(w[k] & 0xffffu);
             p[2 * k + 1] = (u16)(w[k] >> 16);
         }
     }
 }
 
-// 16 finished FP32 values of chunk i0 into the row buffer at swz(i0 + k): four 16-byte stores.
-__device__ __forceinline__ void store16_f32_swz(float* buf, int i0, const float* v) {
+// CH finished FP32 values of chunk i0 into the row buffer at swz(i0 + k).
+template <int CH>
+__device__ __forceinline__ void store_f32_swz(float* buf, int i0, const float* v) {
     float4* b4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-}
-
-// 16 BF16 values from p (16-byte aligned, global or shared; generic loads).
-__device__ __forceinline__ void load_bf16x16_any(const u16* p, float* v) {
-    const uint4* u = reinterpret_cast<const uint4*>(p);
-    const uint4 a = u[0], b = u[1];
-    const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        v[2 * k] = __uint_as_float(w[k] << 16);
-        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-    }
+    for (int q = 0; q < CH / 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
 // ---------------------------------------------------------------------------------------------------- loaders
-// 16 inputs of a row (BF16 / F16 / F32), 16-byte aligned.
-template <int DT>
-__device__ __forceinline__ void load16(const void* p, float* v) {
-    if (DT == TCQ_DT_F32) {
-        const float4* f = reinterpret_cast<const float4*>(p);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 a = __ldg(f + q);
-            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-        }
-    } else {
+// NB bytes (4, 8 or a multiple of 16) from p, aligned to min(NB, 16), as 32-bit words. G: p is global memory the
+// kernel only reads (__ldg); otherwise p may be in any address space (plain loads).
+template <int NB, bool G>
+__device__ __forceinline__ void ldw(const void* p, u32* w) {
+    if (NB >= 16) {
         const uint4* u = reinterpret_cast<const uint4*>(p);
-        const uint4 a = __ldg(u), b = __ldg(u + 1);
-        const u32 w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int q = 0; q < NB / 16; ++q) {
+            const uint4 a = G ? __ldg(u + q) : u[q];
+            w[4 * q] = a.x; w[4 * q + 1] = a.y; w[4 * q + 2] = a.z; w[4 * q + 3] = a.w;
+        }
+    } else if (NB == 8) {
+        const uint2 a = G ? __ldg(reinterpret_cast<const uint2*>(p)) : *reinterpret_cast<const uint2*>(p);
+        w[0] = a.x; w[1] = a.y;
+    } else {
+        w[0] = G ? __ldg(reinterpret_cast<const u32*>(p)) : *reinterpret_cast<const u32*>(p);
+    }
+}
+
+// CH inputs of a row (BF16 / F16 / F32) from global memory.
+template <int DT, int CH>
+__device__ __forceinline__ void loadc(const void* p, float* v) {
+    if (DT == TCQ_DT_F32) {
+        u32 w[CH];
+        ldw<4 * CH, true>(p, w);
+#pragma unroll
+        for (int k = 0; k < CH; ++k) v[k] = __uint_as_float(w[k]);
+    } else {
+        u32 w[CH / 2];
+        ldw<2 * CH, true>(p, w);
+#pragma unroll
+        for (int k = 0; k < CH / 2; ++k) {
             if (DT == TCQ_DT_BF16) {
                 v[2 * k] = __uint_as_float(w[k] << 16);
                 v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
@@ -228,63 +259,55 @@ __device__ __forceinline__ void load16(const void* p, float* v) {
     }
 }
 
-__device__ __forceinline__ void load_signs16(const i8* p, float* sg) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-    const u32 w[4] = {a.x, a.y, a.z, a.w};
+// CH BF16 values from p (global or shared; plain loads).
+template <int CH>
+__device__ __forceinline__ void load_bf16c_any(const u16* p, float* v) {
+    u32 w[CH / 2];
+    ldw<2 * CH, false>(p, w);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
-}
-
-// The same for a vector that may be a shared-memory copy (stage_const): plain, generic loads.
-__device__ __forceinline__ void load_signs16_any(const i8* p, float* sg) {
-    const uint4 a = *reinterpret_cast<const uint4*>(p);
-    const u32 w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
-}
-
-__device__ __forceinline__ void load_f16x(const float* p, float* v) {
-    const float4* f = reinterpret_cast<const float4*>(p);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 a = __ldg(f + q);
-        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+    for (int k = 0; k < CH / 2; ++k) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
     }
 }
 
-__device__ __forceinline__ void load_f16x_any(const float* p, float* v) {
-    const float4* f = reinterpret_cast<const float4*>(p);
+// CH signs (+-1 as int8) as floats; G as in ldw.
+template <int CH, bool G>
+__device__ __forceinline__ void load_signsc(const i8* p, float* sg) {
+    u32 w[CH / 4];
+    ldw<CH, G>(p, w);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 a = f[q];
-        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-    }
+    for (int k = 0; k < CH; ++k) sg[k] = (float)(i8)((w[k >> 2] >> (8 * (k & 3))) & 0xff);
+}
+
+// CH FP32 values; G as in ldw.
+template <int CH, bool G>
+__device__ __forceinline__ void load_f32c(const float* p, float* v) {
+    u32 w[CH];
+    ldw<4 * CH, G>(p, w);
+#pragma unroll
+    for (int k = 0; k < CH; ++k) v[k] = __uint_as_float(w[k]);
 }
 
 // Scaled accumulator inputs z = SCALE(acc): I32 ((float)a * s) * rs, F32 a, BF16 bf2f(a) * rs (kernels.py:545).
 // rs may be a shared-memory copy (stage_const).
-template <int AT>
-__device__ __forceinline__ void load_scaled16(const void* acc, size_t idx, float s, const float* rs, float* v) {
+template <int AT, int CH>
+__device__ __forceinline__ void load_scaledc(const void* acc, size_t idx, float s, const float* rs, float* v) {
     if (AT == TCQ_DT_I32) {
-        const int4* a4 = reinterpret_cast<const int4*>(reinterpret_cast<const int*>(acc) + idx);
-        float r[16];
-        load_f16x_any(rs, r);
+        float r[CH];
+        load_f32c<CH, false>(rs, r);
+        u32 a[CH];
+        ldw<4 * CH, true>(reinterpret_cast<const int*>(acc) + idx, a);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int4 a = __ldg(a4 + q);
-            v[4 * q] = ((float)a.x * s) * r[4 * q];
-            v[4 * q + 1] = ((float)a.y * s) * r[4 * q + 1];
-            v[4 * q + 2] = ((float)a.z * s) * r[4 * q + 2];
-            v[4 * q + 3] = ((float)a.w * s) * r[4 * q + 3];
-        }
+        for (int k = 0; k < CH; ++k) v[k] = ((float)(int)a[k] * s) * r[k];
     } else if (AT == TCQ_DT_F32) {
-        load_f16x(reinterpret_cast<const float*>(acc) + idx, v);
+        load_f32c<CH, true>(reinterpret_cast<const float*>(acc) + idx, v);
     } else {
-        float r[16];
-        load_f16x_any(rs, r);
-        load16<TCQ_DT_BF16>(reinterpret_cast<const u16*>(acc) + idx, v);
+        float r[CH];
+        load_f32c<CH, false>(rs, r);
+        loadc<TCQ_DT_BF16, CH>(reinterpret_cast<const u16*>(acc) + idx, v);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = v[k] * r[k];
+        for (int k = 0; k < CH; ++k) v[k] = v[k] * r[k];
     }
 }
 

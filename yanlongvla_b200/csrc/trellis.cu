@@ -258,18 +258,19 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         for (int m = 0; m < M; ++m) {
             const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
             float mx = 0.f;
-            row_walsh16(sbuf, K,
-                      [&](int cc, float* v) {
-                          float sg[16];
-                          if (xdt == TCQ_DT_BF16) load16<TCQ_DT_BF16>(xr + (size_t)16 * cc * es, v);
-                          else if (xdt == TCQ_DT_F16) load16<TCQ_DT_F16>(xr + (size_t)16 * cc * es, v);
-                          else load16<TCQ_DT_F32>(xr + (size_t)16 * cc * es, v);
-                          load_signs16(su + 16 * cc, sg);
+            // Chunks of 4: a few rows on 512 threads, where per-thread latency bounds the transform.
+            row_walshc<4>(sbuf, K,
+                          [&](int cc, float* v) {
+                              float sg[4];
+                              if (xdt == TCQ_DT_BF16) loadc<TCQ_DT_BF16, 4>(xr + (size_t)4 * cc * es, v);
+                              else if (xdt == TCQ_DT_F16) loadc<TCQ_DT_F16, 4>(xr + (size_t)4 * cc * es, v);
+                              else loadc<TCQ_DT_F32, 4>(xr + (size_t)4 * cc * es, v);
+                              load_signsc<4, true>(su + 4 * cc, sg);
 #pragma unroll
-                          for (int k = 0; k < 16; ++k) v[k] = v[k] * sg[k];
-                      },
-                      [&](int i0, const float* v) { store_chunk(sbuf, i0, v, mx); },
-                      [&](int i, float v) { sbuf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+                              for (int k = 0; k < 4; ++k) v[k] = v[k] * sg[k];
+                          },
+                          [&](int i0, const float* v) { store_chunk<4>(sbuf, i0, v, mx); },
+                          [&](int i, float v) { sbuf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
             quantize_store(sbuf, mx, red, nullptr, sq4, ss, m, K, M);
             __syncthreads();                       // sbuf is rewritten by the next row; sq4 / ss complete
         }
