@@ -13,6 +13,7 @@
 //             epilogue of tile i overlaps the MMAs of tile i + 1.
 // Every mbarrier wait is bounded (about 2 s): on expiry the kernel sets a device error flag, stops, waits (bounded)
 // for its copies and MMAs in flight, frees TMEM and returns; tcq_device_error() reports the flag.
+#include <algorithm>
 #include "tma.cuh"
 #include "trellis_common.cuh"
 
@@ -450,9 +451,11 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
 // stage, 16 decoder warps write the 128 x 128 INT8 A tile in the 128B-swizzled K-major UMMA layout (512 threads x 2
 // tile rows), TMA brings the BN x 128 activation tile, one thread issues four tcgen05.mma.kind::i8 (M = 128, N = BN,
 // K = 32) into TMEM. Epilogue (decoder warps 2..5, one TMEM lane quarter each): scale and store z, or, when K is split
-// over several CTAs, add INT32 partials into the workspace; the CTA that completes a channel tile writes z and zeroes
-// the workspace again (the same exact finish as the small-M kernel).
+// over (at most kTcKsMax) CTAs, store INT32 partials into the split's own slice of the workspace (plain stores: no
+// atomics competing in L2); the CTA whose arrival completes a channel tile sums the slices with all its decoder
+// warps, writes z and zeroes the slices again.
 constexpr int kTcDecWarps = 16;
+constexpr int kTcKsMax = 4;         // K splits per channel tile, at most (the finishing CTA sums that many slices)
 constexpr int kTcThreads = 64 + 32 * kTcDecWarps;
 
 struct TcParts {
@@ -460,7 +463,14 @@ struct TcParts {
     int ks;         // K splits per channel tile
     int kb;         // 128-byte K stages
     int nb0, nb1;   // layer bounds in tile rows (multiples of 8)
+    int cl;         // the K splits of a channel tile are one thread-block cluster (ks > 1, token tiles of 32)
 };
+
+__device__ __forceinline__ int ld_cluster_s32(u32 addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -504,6 +514,29 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     pdl_launch_dependents();
+    // Decoder thread d -> tile (i, j) = (d >> 6, (d >> 3) & 7) of a K stage, tile rows 2g, 2g + 1 (g = d & 7). Its
+    // words of the first stage are requested before the table build (their DRAM latency hides under it), the next
+    // stage's while the current one is decoded.
+    const int dd = threadIdx.x - 64;
+    const int di = dd >> 6, dj = (dd >> 3) & 7, dg = dd & 7;
+    const bool drow_ok = warp >= 2 && tr0 + di < tiles_n;
+    auto load_words = [&](int kb, u32& a, u32& b, u32& c) {
+        const int tc = kb * 8 + dj;
+        a = b = c = 0;
+        if (drow_ok && kb < kb1 && tc < tiles_k) {
+            const u32* tw = reinterpret_cast<const u32*>(bits + ((size_t)(tr0 + di) * tiles_k + tc) * 32);
+            a = __ldg(tw + 2 * dg);
+            b = __ldg(tw + 2 * dg + 1);
+            c = __ldg(tw + ((2 * dg + 2) & 15));
+        }
+    };
+    u32 nw0, nw1, nw2;
+    load_words(kb0, nw0, nw1, nw2);
+    if (threadIdx.x < 8 && tr0 + (int)threadIdx.x < tiles_n && kb1 - kb0 > 1) {   // later stages: into L2 now
+        const int t0 = (kb0 + 1) * 8, t1 = kb1 * 8 < tiles_k ? kb1 * 8 : tiles_k;
+        if (t1 > t0)
+            prefetch_l2_bulk(bits + ((size_t)(tr0 + threadIdx.x) * tiles_k + t0) * 32, (unsigned)(t1 - t0) * 64u);
+    }
     tcq::build_table_i8(tab, pairs, t8 + 1024 * slot);               // weights only: before the dependency wait
     tc_fence_before();
     __syncthreads();
@@ -542,23 +575,16 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             mma_commit(tfull);   // also on an early stop: it arrives once every MMA issued so far has finished
         }
     } else {
-        // ---- decoders: thread d -> tile (i, j) = (d >> 6, (d >> 3) & 7) of the stage, tile rows 2g, 2g + 1 (g = d & 7)
-        const int d = threadIdx.x - 64;
-        const int i = d >> 6, j = (d >> 3) & 7, g = d & 7;
+        // ---- decoders (tile (di, dj), tile rows 2 dg, 2 dg + 1 of each stage; see load_words)
+        const int i = di, j = dj, g = dg;
         const u32 lane4 = 4u * lane;
-        const bool row_ok = tr0 + i < tiles_n;
         int st = 0;
         u32 ph = 0;
         for (int kb = kb0; kb < kb1; ++kb) {
             const int tc = kb * 8 + j;
-            u32 w0 = 0, w1 = 0, w2 = 0;
-            const bool ok = row_ok && tc < tiles_k;
-            if (ok) {
-                const u32* tw = reinterpret_cast<const u32*>(bits + ((size_t)(tr0 + i) * tiles_k + tc) * 32);
-                w0 = __ldg(tw + 2 * g);
-                w1 = __ldg(tw + 2 * g + 1);
-                w2 = __ldg(tw + ((2 * g + 2) & 15));
-            }
+            const u32 w0 = nw0, w1 = nw1, w2 = nw2;
+            const bool ok = drow_ok && tc < tiles_k;
+            load_words(kb + 1, nw0, nw1, nw2);
             if (!mbar_wait(empty0 + 8 * st, ph ^ 1, abort_flag)) break;
             uint8_t* a = sA + st * A_BYTES;
 #pragma unroll
@@ -580,6 +606,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             if (mbar_wait(tfull, 0, abort_flag)) {
                 tc_fence_after();
                 const float r = chok ? rs[ch] : 0.f;
+                int* part = ws_acc + (size_t)ksi * M * N;    // this split's slice of the partial sums
 #pragma unroll 1
                 for (int c = 0; c < (BN + 31) / 32; ++c) {
                     u32 v[32];
@@ -591,7 +618,8 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
                             if (tok < M) {
                                 const size_t o = (size_t)tok * N + ch;
                                 if (P.ks == 1) z[o] = ((float)(int)v[jj] * s_tok[tok]) * r;
-                                else atomicAdd(ws_acc + o, (int)v[jj]);
+                                else if (P.cl) reinterpret_cast<int*>(sA)[tok * BM + 32 * q + lane] = (int)v[jj];
+                                else part[o] = (int)v[jj];
                             }
                         }
                     }
@@ -599,10 +627,43 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             }
         }
     }
-    // Split K: every CTA has added its partials; the one whose arrival completes the channel tile finishes it. The
-    // decision sits between two CTA-wide barriers that every thread reaches on every path.
+    if (P.cl) {
+        // The K splits of a channel tile are one cluster and each left its partial sums in its own shared memory (the
+        // A stages, free once every MMA is done). The leader (rank 0) sums every rank's partials in rank order through
+        // distributed shared memory, 4 elements x ks ranks of loads in flight per thread; the second cluster barrier
+        // keeps the peers' shared memory alive until the leader has read it. Every thread reaches both barriers.
+        cluster_sync();
+        if (cluster_rank() == 0 && !*abort_flag && warp >= 2) {
+            const int t = threadIdx.x - 64;
+            const u32 base = smem_u32(sA);
+            for (int e0 = t; e0 < M * BM; e0 += 4 * 32 * kTcDecWarps) {
+                int vals[4][8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = e0 + u * 32 * kTcDecWarps;
+                    const bool ok = e < M * BM && ct * BM + e % BM < N;
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) vals[u][r] = ok && r < P.ks ? ld_cluster_s32(map_to_rank(base + 4u * e, r)) : 0;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = e0 + u * 32 * kTcDecWarps, tok = e / BM, ch = ct * BM + e % BM;
+                    if (e < M * BM && ch < N) {
+                        int sum = 0;
+#pragma unroll
+                        for (int r = 0; r < 8; ++r)
+                            if (r < P.ks) sum += vals[u][r];
+                        z[(size_t)tok * N + ch] = ((float)sum * s_tok[tok]) * rs[ch];
+                    }
+                }
+            }
+        }
+        cluster_sync();
+    }
+    // Split K without a cluster: every CTA has stored its partials; the one whose arrival completes the channel tile
+    // finishes it. The decision sits between two CTA-wide barriers that every thread reaches on every path.
     __syncthreads();
-    if (P.ks > 1 && threadIdx.x == 0) {
+    if (P.ks > 1 && !P.cl && threadIdx.x == 0) {
         int done = 0;
         if (!*abort_flag) {
             int old;
@@ -613,14 +674,34 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         *last_flag = done;
     }
     __syncthreads();
-    if (P.ks > 1 && *last_flag && warp >= 4 && warp < 8) {
-        const int ch = ct * BM + 32 * (warp & 3) + lane;
-        if (ch < N) {
-            const float r = rs[ch];
-            for (int tok = 0; tok < M; ++tok) {
-                const size_t o = (size_t)tok * N + ch;
-                const int vv = atomicExch(ws_acc + o, 0);
-                z[o] = ((float)vv * s_tok[tok]) * r;
+    if (P.ks > 1 && !P.cl && *last_flag && warp >= 2) {
+        // The CTA that completes the channel tile sums its ks slices (exact integers, slice order), clears them for the
+        // next call and writes z. All 16 decoder warps take part, 8 elements (tok, channel) per thread and step with
+        // every load of the step issued before any is used; consecutive threads take consecutive channels.
+        const int t = threadIdx.x - 64;
+        for (int e0 = t; e0 < M * BM; e0 += 8 * 32 * kTcDecWarps) {
+            int vals[8][kTcKsMax];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int e = e0 + u * 32 * kTcDecWarps, tok = e / BM, ch = ct * BM + e % BM;
+                const bool ok = e < M * BM && ch < N;
+#pragma unroll
+                for (int k = 0; k < kTcKsMax; ++k)
+                    vals[u][k] = ok && k < P.ks ? __ldcg(ws_acc + ((size_t)k * M + tok) * N + ch) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int e = e0 + u * 32 * kTcDecWarps, tok = e / BM, ch = ct * BM + e % BM;
+                if (e < M * BM && ch < N) {
+                    int sum = 0;
+#pragma unroll
+                    for (int k = 0; k < kTcKsMax; ++k)
+                        if (k < P.ks) {
+                            sum += vals[u][k];
+                            ws_acc[((size_t)k * M + tok) * N + ch] = 0;
+                        }
+                    z[(size_t)tok * N + ch] = ((float)sum * s_tok[tok]) * rs[ch];
+                }
             }
         }
     }
@@ -731,6 +812,34 @@ int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, co
     return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
 }
 
+// Clusters of `size` CTAs of `kern` (smem bytes each) that can be resident at once (cached per kernel and size).
+template <class Kern>
+int max_clusters(Kern kern, int smem, int size) {
+    static int cache[9] = {0};
+    static const void* cached_for = nullptr;
+    if (size < 2 || size > 8) return 0;
+    if (cached_for != reinterpret_cast<const void*>(kern)) {
+        for (int& c : cache) c = 0;
+        cached_for = reinterpret_cast<const void*>(kern);
+    }
+    if (cache[size] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(size * 64);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = size;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        cache[size] = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0 ? n : -1;
+    }
+    return cache[size];
+}
+
 template <int BN, int STAGES>
 int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z, int M, int N,
               int K, int nb0, int nb1, int* ws, cudaStream_t st) {
@@ -742,10 +851,24 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     TcParts P;
     P.ct = (N + BM - 1) / BM;
     P.kb = (K + BK - 1) / BK;
-    int ks = sms() / P.ct;
-    if (ks < 1) ks = 1;
-    if (ks > P.kb) ks = P.kb;
+    // K splits. Token tiles of 32: the splits of a channel tile form a cluster (at most 8, a portable size) that
+    // reduces in distributed shared memory: the largest split with at least 3 K stages per CTA whose clusters are all
+    // resident at once (one CTA fills an SM, so clusters pack into the GPCs only so far). Otherwise, and for wider
+    // token tiles, the splits reduce through workspace slices (at most kTcKsMax).
+    int ks = 1;
+    bool cl = false;
+    if (BN == 32) {
+        int c = std::min({8, sms() / P.ct, P.kb, (P.kb + 2) / 3});
+        for (; c >= 2; --c)
+            if (P.ct <= max_clusters(kern, smem, c)) break;
+        if (c >= 2) {
+            ks = c;
+            cl = true;
+        }
+    }
+    if (!cl) ks = std::max(1, std::min({kTcKsMax, sms() / P.ct, P.kb}));
     P.ks = ks;
+    P.cl = cl ? 1 : 0;
     P.nb0 = nb0;
     P.nb1 = nb1;
     cudaLaunchConfig_t cfg = {};
@@ -753,13 +876,20 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = P.cl ? P.ks : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = P.cl ? 2 : 1;
+    // Workspace: the channel tiles' arrival counters, then kTcKsMax slices of (M, N) INT32 partial sums.
+    int* cnt = ws;
+    int* part = ws + ((P.ct + 31) & ~31);
     return cudaLaunchKernelEx(&cfg, kern, tmQ, reinterpret_cast<const u16*>(bits), reinterpret_cast<const i8*>(t8), s, rs, z, M, N,
-                              K, P, ws, ws + (size_t)M * N) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+                              K, P, part, cnt) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
 }
 
 int check_args(const int8_t* q, const int8_t* W, const void* out, int M, int N, int K) {
@@ -792,7 +922,7 @@ int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const fl
 
 size_t tcq_gemm_tcq_tc_workspace(int M, int N) {
     if (M <= 0 || N <= 0) return 0;
-    return ((size_t)M * N + (size_t)((N + BM - 1) / BM)) * sizeof(int);
+    return ((size_t)kTcKsMax * M * N + (size_t)(((N + BM - 1) / BM + 31) & ~31)) * sizeof(int);
 }
 
 int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const float* s, const float* rs, float* z, int M, int N,

@@ -58,7 +58,7 @@ k_gemmf_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const u16* 
         if (sl != slot) {                           // uniform over the block
             __syncthreads();                        // the previous table is no longer read
             if (threadIdx.x < 64)
-                reinterpret_cast<uint4*>(pairs)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(t8 + 1024 * sl) + threadIdx.x);
+                reinterpret_cast<uint4*>(pairs)[threadIdx.x] = ldg_table_v4(reinterpret_cast<const uint4*>(t8 + 1024 * sl) + threadIdx.x);
             __syncthreads();
             fill_table_bf16_from_i8(tab, pairs);
             __syncthreads();

@@ -124,11 +124,33 @@ TCQ_HD uint4 ldg_nc_v4(const void* p) {
     return r;
 }
 
-// Streaming load that does not allocate in L1 (the 2-bit weight stream is read exactly once per launch).
+// L2 eviction priorities of the decode kernels' two kinds of input: the weight stream is read once per launch (evict
+// first); the per-layer 1 KB decode tables are read by every CTA of every launch of their layer (evict last), so they
+// stay in L2 while the weight streams of the layers in between pass through.
+TCQ_HD u64 l2_evict_first() {
+    u64 pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+TCQ_HD u64 l2_evict_last() {
+    u64 pol;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Streaming load of the weight stream: no L1 allocation, L2 evict-first.
 TCQ_HD uint4 ldg_stream_v4(const void* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(l2_evict_first()));
+    return r;
+}
+
+// Load of a decode table: L2 evict-last.
+TCQ_HD uint4 ldg_table_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(l2_evict_last()));
     return r;
 }
 

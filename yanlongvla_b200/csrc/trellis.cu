@@ -202,7 +202,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     // The 1 KB table is the CTA's first memory request: the table build waits for it, and under a full HBM stream
     // a request queued behind this CTA's weight loads returns about a microsecond later.
     uint4 t8v = make_uint4(0, 0, 0, 0);
-    if (threadIdx.x < 64) t8v = __ldg(reinterpret_cast<const uint4*>(t8 + 1024 * slot) + threadIdx.x);
+    if (threadIdx.x < 64) t8v = ldg_table_v4(reinterpret_cast<const uint4*>(t8 + 1024 * slot) + threadIdx.x);
     // The CTAs of a launch start one by one, in index order, as the previous launch's CTAs leave their SMs (over
     // about one launch time). When each CTA has little work, CTA c asks L2 for the stream of CTA c + pf_lead, which
     // starts about a DRAM latency later and then finds its weights in L2 instead of waiting on DRAM.
@@ -373,13 +373,17 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         if (lane == 0) last = atom_add_acq_rel_gpu(ws_cnt + trow, mine) + mine == S;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-            for (int i = lane; i < RV; i += 32) {
-                const int rr = i / MT, m = i % MT, row = trow * 16 + rr;
-                if (m < M) {
-                    const size_t o = (size_t)m * N + row;
-                    const int v = atomicExch(ws_acc + o, 0);      // read and clear; lanes issue these in parallel
-                    z[o] = ((float)v * ss[m]) * rsr[rr];
-                }
+            constexpr int IT = (RV + 31) / 32;
+            int v[IT];
+#pragma unroll
+            for (int j = 0; j < IT; ++j) {                // read and clear: all of a lane's requests in flight at once
+                const int i = lane + 32 * j, rr = i / MT, m = i % MT;
+                v[j] = i < RV && m < M ? atomicExch(ws_acc + (size_t)m * N + trow * 16 + rr, 0) : 0;
+            }
+#pragma unroll
+            for (int j = 0; j < IT; ++j) {
+                const int i = lane + 32 * j, rr = i / MT, m = i % MT;
+                if (i < RV && m < M) z[(size_t)m * N + trow * 16 + rr] = ((float)v[j] * ss[m]) * rsr[rr];
             }
             if (lane == 0) ws_cnt[trow] = 0;
         }

@@ -15,7 +15,7 @@ constexpr int kTabBytes = 1024 * 32 * 4;   // per-lane replicated decode table
 // 16-byte load per thread (one memory round trip), then the 128 KB replicated table is written with consecutive
 // 16-byte stores (lanes of a warp cover 512 contiguous bytes: no bank conflicts).
 __device__ __forceinline__ void stage_pairs(u16* pairs, const void* __restrict__ src) {
-    if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = __ldg(reinterpret_cast<const uint4*>(src) + threadIdx.x);
+    if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = ldg_table_v4(reinterpret_cast<const uint4*>(src) + threadIdx.x);
     __syncthreads();
 }
 

@@ -1,7 +1,9 @@
 """Kernel-class breakdown of one CUDA-graph replay (the reference's runner.kernel_classes, runner.py:227-266).
 
 A torch.profiler (CUPTI) trace of a single replay; device time per kernel class, launch counts, wall time and the
-gaps between kernels. Classes are matched by regex on the kernel name, first match wins.
+gaps between kernels, plus each class's share of the critical path (a kernel's time from the previous kernel's end to
+its own end: with programmatic dependent launch a kernel's own time range includes its wait for the predecessor).
+Classes are matched by regex on the kernel name, first match wins.
 """
 import re
 from collections import Counter, defaultdict
@@ -40,18 +42,29 @@ def kernel_classes(graph, warm=3):
         end.synchronize()
     wall = start.elapsed_time(end)
     by, launches, top = defaultdict(float), Counter(), Counter()
-    for e in prof.events():
-        if e.device_type.name != 'CUDA':
-            continue
+    excl, excl_top = defaultdict(float), Counter()
+    kernels = sorted((e for e in prof.events() if e.device_type.name == 'CUDA'), key=lambda e: e.time_range.start)
+    prev_end = None
+    for e in kernels:
         dur = e.time_range.elapsed_us() / 1000
         cls = next(c for c, pat in CLASSES if re.search(pat, e.name))
         by[cls] += dur
         launches[cls] += 1
         top[e.name[:90]] += dur
+        # Kernels launched early by programmatic dependent launch wait for their predecessor inside their own time
+        # range, so a kernel's share of the critical path is the time from the previous kernel's end to its own end.
+        t0, t1 = e.time_range.start, e.time_range.end
+        x = (t1 - max(t0, prev_end if prev_end is not None else t0)) / 1000
+        if x > 0:
+            excl[cls] += x
+            excl_top[e.name[:90]] += x
+        prev_end = t1 if prev_end is None else max(prev_end, t1)
     total = sum(by.values())
-    return dict(wall_ms=wall, kernel_ms=total, gaps_ms=max(wall - total, 0.0), launches=sum(launches.values()),
+    return dict(wall_ms=wall, kernel_ms=total, gaps_ms=max(wall - sum(excl.values()), 0.0), launches=sum(launches.values()),
                 by_class_ms={k: round(v, 3) for k, v in sorted(by.items(), key=lambda kv: -kv[1])},
-                launches_by_class=dict(launches), top=[(nm, round(d, 3)) for nm, d in top.most_common(12)])
+                critical_path_ms_by_class={k: round(v, 3) for k, v in sorted(excl.items(), key=lambda kv: -kv[1])},
+                launches_by_class=dict(launches), top=[(nm, round(d, 3)) for nm, d in top.most_common(12)],
+                critical_path_top=[(nm, round(d, 3)) for nm, d in excl_top.most_common(16)])
 
 
 # ----------------------------------------------------------------------------------------------- profiling cases
@@ -59,6 +72,7 @@ def kernel_classes(graph, warm=3):
 #   python -m yanlongvla_b200.profile gemv [--n 4096] [--k 4096] [--tokens 1] [--launches 4]
 #   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--launches 4]
 #   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
+#   python -m yanlongvla_b200.profile chain [--m 17] [--k 1536] [--launches 6]
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
 # kernels.int_mm on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
@@ -106,10 +120,27 @@ def _case_rows(kind, m, k, launches):
             K.rotate(x, su, out=y)
 
 
+def _case_chain(m, n, launches):
+    """kernels.chain at a DiT block boundary: FP32 z of the previous layer -> post -> residual add -> RMSNorm -> the
+    next layer's pre (INT8 + scales)."""
+    from . import kernels as K
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(14)
+    x = torch.randn(m, n, device=dev, generator=g).bfloat16()
+    z = torch.randn(m, n, device=dev, generator=g)
+    w = (torch.rand(n, device=dev, generator=g) + 0.5).bfloat16()
+    sv = (torch.randint(0, 2, (n,), device=dev, generator=g) * 2 - 1).to(torch.int8)
+    su = (torch.randint(0, 2, (n,), device=dev, generator=g) * 2 - 1).to(torch.int8)
+    q = torch.empty(m, n, dtype=torch.int8, device=dev)
+    s = torch.empty(m, device=dev)
+    for _ in range(launches):
+        K.chain(x, 'rms', w, None, 1e-6, acc=z, sv=sv, su=su, q=q, scale=s, want_n=False)
+
+
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description='one kernel case for a profiler')
-    ap.add_argument('case', choices=['gemv', 'gemm', 'pre', 'rotate'])
+    ap.add_argument('case', choices=['gemv', 'gemm', 'pre', 'rotate', 'chain'])
     ap.add_argument('--m', type=int, default=4096)
     ap.add_argument('--n', type=int, default=None)
     ap.add_argument('--k', type=int, default=None)
@@ -120,6 +151,8 @@ def main(argv=None):
         _case_gemv(a.n or 4096, a.k or 4096, a.tokens, a.launches)
     elif a.case == 'gemm':
         _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches)
+    elif a.case == 'chain':
+        _case_chain(a.m, a.k or 1536, a.launches)
     else:
         _case_rows(a.case, a.m, a.k or 4096, a.launches)
     torch.cuda.synchronize()
