@@ -73,6 +73,7 @@ def kernel_classes(graph, warm=3):
 #   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--launches 4]
 #   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
 #   python -m yanlongvla_b200.profile chain [--m 17] [--k 1536] [--launches 6]
+#   python -m yanlongvla_b200.profile gemv_tc [--n 1536] [--k 1536] [--tokens 17] [--launches 4]
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
 # kernels.int_mm on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
@@ -90,6 +91,23 @@ def _case_gemv(n, k, tokens, launches):
     t8, rs = t8.contiguous(), rs.contiguous()
     for _ in range(launches):
         K.gemm_tcq(bits, t8, q4, s, rs, z, k)
+
+
+def _case_gemv_tc(n, k, tokens, launches):
+    """kernels.gemm_tcq_tc (tensor-core fused decode-GEMM) on one trellis layer and `tokens` INT8 token rows."""
+    from . import kernels as K
+    from .tcq_format import snap
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(15)
+    bits = torch.randint(-32768, 32768, ((n // 16) * (k // 16), 32), dtype=torch.int32, device=dev, generator=g).to(torch.int16)
+    t8, rs, _ = snap((torch.randn(512, 2, device=dev, generator=g) * 0.968).half(),
+                     (torch.rand(n, device=dev, generator=g) * 0.02 + 0.005).half())
+    q = torch.randint(-127, 128, (tokens, k), dtype=torch.int8, device=dev, generator=g)
+    s = torch.rand(tokens, device=dev, generator=g)
+    z = torch.empty(tokens, n, device=dev)
+    t8, rs = t8.contiguous(), rs.contiguous()
+    for _ in range(launches):
+        K.gemm_tcq_tc(bits, t8, q, s, rs, z, k)
 
 
 def _case_gemm(m, k, n, launches):
@@ -140,7 +158,7 @@ def _case_chain(m, n, launches):
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description='one kernel case for a profiler')
-    ap.add_argument('case', choices=['gemv', 'gemm', 'pre', 'rotate', 'chain'])
+    ap.add_argument('case', choices=['gemv', 'gemv_tc', 'gemm', 'pre', 'rotate', 'chain'])
     ap.add_argument('--m', type=int, default=4096)
     ap.add_argument('--n', type=int, default=None)
     ap.add_argument('--k', type=int, default=None)
@@ -149,6 +167,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.case == 'gemv':
         _case_gemv(a.n or 4096, a.k or 4096, a.tokens, a.launches)
+    elif a.case == 'gemv_tc':
+        _case_gemv_tc(a.n or 1536, a.k or 1536, a.tokens, a.launches)
     elif a.case == 'gemm':
         _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches)
     elif a.case == 'chain':
