@@ -158,6 +158,15 @@ int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int
 int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype,
                   int M, int N, int K, void* stream);
 
+/* tcq_int8_gemm with BF16 output and the layer's bias (and activation) in the epilogue (no counterpart in the
+ * reference, whose vision tower is not W8A8: this is the W8A8 Linear of the policy's vision tower, followed there by a
+ * BF16 tensor add of its bias and, for the MLP's first layer, the tanh GELU): out = act(BF16(BF16(z) + bias)),
+ * z = ((float)acc * s_tok[t]) * s_ch[n], i.e. the result of int8_gemm, then `+ bias`, then the activation, in PyTorch
+ * BF16 arithmetic bit for bit. bias (N,) BF16 or NULL; act_lut the 65536-entry BF16 table of the activation
+ * (kernels.act_table) or NULL. */
+int tcq_int8_gemm_bias(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, const uint16_t* bias,
+                       const uint16_t* act_lut, uint16_t* out, int M, int N, int K, void* stream);
+
 /* Workspace of tcq_gemm_tcq_tc in bytes for (M, N); same zero-filled contract as tcq_gemm_tcq_workspace. */
 size_t tcq_gemm_tcq_tc_workspace(int M, int N);
 

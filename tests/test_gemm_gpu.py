@@ -151,6 +151,26 @@ def test_int8_gemm_vision_shapes(K, M, Kd, N):
     assert np.array_equal(n(out), O.int8_gemm_scaled(q, w, s[:, 0], sc))
 
 
+@pytest.mark.parametrize('act', [None, 'gelu'])
+@pytest.mark.parametrize('M,Kd,N', [(7, 1152, 1152), (40, 1152, 4304), (512, 1152, 4304), (2048, 1152, 1152)])
+def test_int8_gemm_bias_act_equals_torch_ops(K, M, Kd, N, act):
+    """The vision Linear's epilogue: act(BF16(BF16(z) + bias)) in the GEMM equals int8_gemm, then the PyTorch BF16
+    bias add, then the PyTorch activation, bit for bit (small-M tiles, split tiles and the two-SM path)."""
+    r = cases.rng('vitb', M, Kd, N)
+    a = (r.standard_normal((M, Kd)) * 2).astype(np.float32)
+    w = r.integers(-127, 128, size=(N, Kd), dtype=np.int32).astype(np.int8)
+    sc = r.uniform(1e-4, 1e-3, N).astype(np.float32)
+    q, s = O.quantize_tokens(a)
+    bias = torch.from_numpy((r.standard_normal(N) * 0.5).astype(np.float32)).cuda().bfloat16()
+    want = K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc)) + bias
+    if act == 'gelu':
+        want = torch.nn.functional.gelu(want, approximate='tanh')
+    got = K.int8_gemm_bias(t(q), t(w), t(s[:, 0].copy()), t(sc), bias=bias, act=act)
+    assert torch.equal(got, want)
+    plain = K.int8_gemm_bias(t(q), t(w), t(s[:, 0].copy()), t(sc))
+    assert torch.equal(plain, K.int8_gemm(t(q), t(w), t(s[:, 0].copy()), t(sc)))
+
+
 def test_bounded_wait_expires_and_reports(K):
     """The failure path of the bounded waits, without a fault: a wait on a barrier nothing arrives at gives up after
     10 ms and raises the device error flag; the flag clears and the context keeps working."""

@@ -41,6 +41,7 @@ SIGNATURES = {
     'tcq_gemm_tcq_tc': [P, P, P, P, P, P, I, I, I, I, I, P, SZ, P],
     'tcq_int_mm': [P, P, P, I, I, I, P],
     'tcq_int8_gemm': [P, P, P, P, P, I, I, I, I, P],
+    'tcq_int8_gemm_bias': [P, P, P, P, P, P, P, I, I, I, P],
     'tcq_gemmf_tcq': [P, P, P, P, P, I, I, I, I, I, I, P],
     'tcq_gemmf_w8': [P, P, P, P, I, I, I, I, P],
     'tcq_add_norm': [P, P, P, P, P, P, I, P, P, I, I, F, I, I, I, P],

@@ -25,7 +25,8 @@ using namespace tcq;
 
 constexpr int BM = 128;           // channels per tile
 constexpr int BK = 128;           // K bytes per stage
-constexpr int kThreads = 192;
+constexpr int kEpiWarps1 = 8;                // single-SM GEMM: two epilogue warps per TMEM lane quarter
+constexpr int kThreads1 = 64 + 32 * kEpiWarps1;
 
 // Bounded wait that reports through this file's device error flag.
 __device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, volatile int* abort_flag, unsigned long long limit = kWaitNs) {
@@ -75,10 +76,86 @@ __device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&v)[32]) {
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_BF16 = 2 };
 
+constexpr int kEpiStageBytes = 32 * 32 * 4;   // per epilogue warp: one 32-token x 32-channel box of the output
+
+// One epilogue step of a warp: TMEM column group v of its lane's channel ch0 + lane, tokens t0 .. t0 + 31, into the
+// output: INT32 as is, or z = ((float)acc * s_tok[t]) * s_ch[n] as FP32 or BF16 (BF16 then + bias as a BF16 tensor add,
+// then the activation table: the PyTorch ops of a biased layer, bit for bit). The token scales come in one coalesced
+// load and go round the warp by shuffles. tma: the values are written token-major into the warp's staging box and one
+// TMA store writes the box (rows past M, columns past N clipped by the tensor map), instead of 32 two- or four-byte
+// stores per lane with stride N.
+template <int MODE, bool SPLIT>
+__device__ __forceinline__ void epi_chunk(const u32 (&v)[32], int lane, int ch0, int t0, int M, int N, float sc, float bb,
+                                          const float* __restrict__ s_tok, const u16* __restrict__ bias,
+                                          const u16* __restrict__ lut, void* __restrict__ out, uint8_t* stage,
+                                          const CUtensorMap* tmO, bool tma) {
+    const int ch = ch0 + lane;
+    const float stv = MODE != OUT_I32 && t0 + lane < M ? s_tok[t0 + lane] : 0.f;
+    auto value = [&](int j, float st) -> u32 {
+        if (MODE == OUT_I32) return v[j];
+        const float z = ((float)(int)v[j] * st) * sc;
+        if (MODE == OUT_F32) return __float_as_uint(z);
+        u16 y = f2bf(z);
+        if (bias) y = f2bf(bf2f(y) + bb);
+        if (lut) y = lut[y];
+        return y;
+    };
+    if (tma && !SPLIT) {
+        if (lane == 0) bulk_wait_read_all();       // the warp's previous box has left the staging area
+        __syncwarp();
+        if (MODE == OUT_BF16) {
+            // Two tokens at a time: one paired round-to-nearest conversion (f2bf2) for the product and one for the
+            // bias add, the same roundings as f2bf on each value.
+            u16* st16 = reinterpret_cast<u16*>(stage);
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float s0 = __shfl_sync(0xffffffffu, stv, j), s1 = __shfl_sync(0xffffffffu, stv, j + 1);
+                u32 w = f2bf2(((float)(int)v[j] * s0) * sc, ((float)(int)v[j + 1] * s1) * sc);
+                if (bias) w = f2bf2(__uint_as_float(w << 16) + bb, __uint_as_float(w & 0xffff0000u) + bb);
+                if (lut) w = (u32)lut[w & 0xffffu] | ((u32)lut[w >> 16] << 16);
+                st16[j * 32 + lane] = (u16)(w & 0xffffu);
+                st16[(j + 1) * 32 + lane] = (u16)(w >> 16);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float st = __shfl_sync(0xffffffffu, stv, j);
+                reinterpret_cast<u32*>(stage)[j * 32 + lane] = value(j, st);
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> the TMA store
+        __syncwarp();
+        if (lane == 0 && ch0 < N && t0 < M) {
+            tma_store_2d(tmO, smem_u32(stage), ch0, t0);
+            bulk_commit_group();
+        }
+        return;
+    }
+    const bool chok = ch < N;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float st = __shfl_sync(0xffffffffu, stv, j);
+        const int tok = t0 + j;
+        if (chok && tok < M) {
+            const size_t o = (size_t)tok * N + ch;
+            const u32 y = value(j, st);
+            if (MODE == OUT_I32) {
+                if (!SPLIT) reinterpret_cast<int*>(out)[o] = (int)y;
+                else atomicAdd(reinterpret_cast<int*>(out) + o, (int)y);
+            } else if (MODE == OUT_F32) {
+                reinterpret_cast<u32*>(out)[o] = y;
+            } else {
+                reinterpret_cast<u16*>(out)[o] = (u16)y;
+            }
+        }
+    }
+}
+
 template <int BN, int STAGES, int MODE, bool SPLIT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads1, 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
-          const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K, int ks) {
+          const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K, int ks,
+          const u16* __restrict__ bias, const u16* __restrict__ lut, const __grid_constant__ CUtensorMap tmO, int tma) {
     constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
     constexpr u32 TMEM_COLS = 2 * BN;          // two accumulator buffers; BN in {32, 64, 128, 256} -> power of two
     constexpr u32 IDESC = idesc_i8(BN);
@@ -86,7 +163,8 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
-    u64* bars = reinterpret_cast<u64*>(sB + STAGES * B_BYTES);
+    uint8_t* sE = sB + STAGES * B_BYTES;                     // epilogue staging boxes (warps 2..9)
+    u64* bars = reinterpret_cast<u64*>(sE + kEpiWarps1 * kEpiStageBytes);
     u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * STAGES + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
@@ -104,7 +182,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 128);
+            mbar_init(tempty0 + 8 * a, 32 * kEpiWarps1);    // every thread of the epilogue warps
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -185,6 +263,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
         }
     } else {
         const int q = warp & 3;                  // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;        // its share of the tile's 32-token column groups: every other one
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const int a = it & 1;
@@ -192,35 +271,21 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
             if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
             tc_fence_after();
             const int tt = tile / ks, tn = tt % tiles_n, tm = tt / tiles_n;
-            const int ch = tn * BM + 32 * q + lane, m0 = tm * BN;
+            const int ch0 = tn * BM + 32 * q, ch = ch0 + lane, m0 = tm * BN;
             const bool chok = ch < N;
             const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
+            const float bb = (MODE == OUT_BF16 && bias && chok) ? bf2f(bias[ch]) : 0.f;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = half; c < BN / 32; c += 2) {
                 u32 v[32];
                 tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * BN + 32 * c), v);
-                const int t0 = m0 + 32 * c;
-                if (chok) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int tok = t0 + j;
-                        if (tok < M) {
-                            const size_t o = (size_t)tok * N + ch;
-                            if (MODE == OUT_I32) {
-                                if (!SPLIT) reinterpret_cast<int*>(out)[o] = (int)v[j];
-                                else atomicAdd(reinterpret_cast<int*>(out) + o, (int)v[j]);
-                            } else {
-                                const float z = ((float)(int)v[j] * s_tok[tok]) * sc;
-                                if (MODE == OUT_F32) reinterpret_cast<float*>(out)[o] = z;
-                                else reinterpret_cast<u16*>(out)[o] = f2bf(z);
-                            }
-                        }
-                    }
-                }
+                epi_chunk<MODE, SPLIT>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, s_tok, bias, lut, out,
+                                       sE + (warp - 2) * kEpiStageBytes, &tmO, tma != 0);
             }
             tc_fence_before();
             mbar_arrive(tempty0 + 8 * a);
         }
+        if (tma && lane == 0) bulk_wait_all();      // the TMA stores are complete before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
@@ -256,6 +321,8 @@ __global__ void k_wait_expiry(unsigned long long limit_ns) {
 // (tokens) from its own TMEM and releases the buffer on the leader's barrier with a remote arrive.
 constexpr int kStages2 = 6;
 constexpr int kHalf = 128;                                   // channels / tokens per CTA of the pair
+constexpr int kEpiWarps2 = 8;                                // epilogue warps: two per TMEM lane quarter, each half the tokens
+constexpr int kThreads2 = 64 + 32 * kEpiWarps2;
 
 __device__ __forceinline__ u32 cluster_rank() {
     u32 r;
@@ -300,9 +367,10 @@ constexpr u32 idesc_i8_pair() {
 }
 
 template <int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
-              const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K) {
+              const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K,
+              const u16* __restrict__ bias, const u16* __restrict__ lut, const __grid_constant__ CUtensorMap tmO, int tma) {
     constexpr int A_BYTES = kHalf * BK, B_BYTES = kHalf * BK;
     constexpr u32 TMEM_COLS = 512;                           // two 256-column accumulators
     constexpr u32 IDESC = idesc_i8_pair();
@@ -310,7 +378,8 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + kStages2 * A_BYTES;
-    u64* bars = reinterpret_cast<u64*>(sB + kStages2 * B_BYTES);
+    uint8_t* sE = sB + kStages2 * B_BYTES;                   // epilogue staging boxes (warps 2..9)
+    u64* bars = reinterpret_cast<u64*>(sE + kEpiWarps2 * kEpiStageBytes);
     u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * kStages2 + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages2), tfull0 = smem_u32(bars + 2 * kStages2),
@@ -329,7 +398,7 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);                    // the leader's MMA commit (multicast)
-            mbar_init(tempty0 + 8 * a, 8);                   // 4 epilogue warps x 2 CTAs (used in the leader)
+            mbar_init(tempty0 + 8 * a, 2 * kEpiWarps2);     // the epilogue warps of both CTAs (used in the leader)
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -399,6 +468,7 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
         }
     } else {
         const int q = warp & 3;                              // TMEM lane quarter this warp may access
+        const int c0 = ((warp - 2) >> 2) * (256 / 32 / 2);   // its half of the tile's 32-token column groups
         const u32 tempty_leader = map_to_rank(tempty0, 0);
         int it = 0;
         for (int tile = pair; tile < tiles; tile += pairs, ++it) {
@@ -407,35 +477,22 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
             if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
             tc_fence_after();
             const int tn = tile % tiles_n, tm = tile / tiles_n;
-            const int ch = tn * 256 + (int)rank * kHalf + 32 * q + lane, m0 = tm * 256;
+            const int ch0 = tn * 256 + (int)rank * kHalf + 32 * q, ch = ch0 + lane, m0 = tm * 256;
             const bool chok = ch < N;
             const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
+            const float bb = (MODE == OUT_BF16 && bias && chok) ? bf2f(bias[ch]) : 0.f;
 #pragma unroll 1
-            for (int c = 0; c < 256 / 32; ++c) {
+            for (int c = c0; c < c0 + 256 / 32 / 2; ++c) {
                 u32 v[32];
                 tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * 256 + 32 * c), v);
-                const int t0 = m0 + 32 * c;
-                if (chok) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int tok = t0 + j;
-                        if (tok < M) {
-                            const size_t o = (size_t)tok * N + ch;
-                            if (MODE == OUT_I32) {
-                                reinterpret_cast<int*>(out)[o] = (int)v[j];
-                            } else {
-                                const float z = ((float)(int)v[j] * s_tok[tok]) * sc;
-                                if (MODE == OUT_F32) reinterpret_cast<float*>(out)[o] = z;
-                                else reinterpret_cast<u16*>(out)[o] = f2bf(z);
-                            }
-                        }
-                    }
-                }
+                epi_chunk<MODE, false>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, s_tok, bias, lut, out,
+                                       sE + (warp - 2) * kEpiStageBytes, &tmO, tma != 0);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) remote_arrive(tempty_leader + 8 * a);
         }
+        if (tma && lane == 0) bulk_wait_all();      // the TMA stores are complete before the CTA exits
     }
     tc_fence_before();
     cluster_sync();                                          // every MMA done, every TMEM read done in both CTAs
@@ -743,20 +800,38 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows)
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The output as a TMA store target: (M, N) INT32 / FP32 / BF16 row-major, 32 x 32 boxes, no swizzle. False when the
+// address or the row pitch is not a multiple of 16 bytes (the epilogue then stores directly).
+bool make_out_map(CUtensorMap* map, void* out, int M, int N, int mode) {
+    EncodeTiledFn enc = encode_fn();
+    const size_t es = mode == OUT_BF16 ? 2 : 4;
+    if (!enc || !tcq_aligned(out, 16) || ((size_t)N * es) % 16) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)N * es};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = mode == OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : mode == OUT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_INT32;
+    return enc(map, dt, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int STAGES, int MODE, bool SPLIT = false>
 int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K, int ks,
-              cudaStream_t st) {
+              cudaStream_t st, const u16* bias = nullptr, const u16* lut = nullptr) {
     CUtensorMap tmW, tmQ;
     if (!make_map(&tmW, W, N, K, BM) || !make_map(&tmQ, q, M, K, BN)) return TCQ_ERR_ARG;
+    CUtensorMap tmO = {};
+    const int tma = !SPLIT && make_out_map(&tmO, out, M, N, MODE) ? 1 : 0;
     auto kern = k_gemm_i8<BN, STAGES, MODE, SPLIT>;
-    const int smem = 1024 + STAGES * (BM + BN) * BK + (2 * STAGES + 4) * 8 + 16;
+    const int smem = 1024 + STAGES * (BM + BN) * BK + kEpiWarps1 * kEpiStageBytes + (2 * STAGES + 4) * 8 + 16;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
     if (ks > 1 && cudaMemsetAsync(out, 0, (size_t)M * N * sizeof(int), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
     const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN) * ks;
     const int grid = tiles < sms() ? tiles : sms();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kThreads1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -764,23 +839,26 @@ int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K, ks) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K, ks, bias, lut, tmO, tma) == cudaSuccess ? TCQ_OK
+                                                                                                          : TCQ_ERR_LAUNCH;
 }
 
 template <int MODE>
 int launch_i8_2sm(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
-                  cudaStream_t st) {
+                  cudaStream_t st, const u16* bias = nullptr, const u16* lut = nullptr) {
     CUtensorMap tmW, tmQ;
     if (!make_map(&tmW, W, N, K, kHalf) || !make_map(&tmQ, q, M, K, kHalf)) return TCQ_ERR_ARG;
+    CUtensorMap tmO = {};
+    const int tma = make_out_map(&tmO, out, M, N, MODE) ? 1 : 0;
     auto kern = k_gemm_i8_2sm<MODE>;
-    const int smem = 1024 + kStages2 * 2 * kHalf * BK + (2 * kStages2 + 4) * 8 + 16;
+    const int smem = 1024 + kStages2 * 2 * kHalf * BK + kEpiWarps2 * kEpiStageBytes + (2 * kStages2 + 4) * 8 + 16;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
     const int tiles = ((N + 255) / 256) * ((M + 255) / 256);
     int pairs = sms() / 2;
     if (pairs > tiles) pairs = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kThreads2);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -788,7 +866,8 @@ int launch_i8_2sm(const int8_t* q, const int8_t* W, void* out, const float* s_to
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K) == cudaSuccess ? TCQ_OK : TCQ_ERR_LAUNCH;
+    return cudaLaunchKernelEx(&cfg, kern, tmW, tmQ, out, s_tok, s_ch, M, N, K, bias, lut, tmO, tma) == cudaSuccess ? TCQ_OK
+                                                                                                     : TCQ_ERR_LAUNCH;
 }
 
 // Above that, token-tile width: 256 while that still gives a quarter of the SMs a tile (wide tiles re-read the weights least);
@@ -796,20 +875,20 @@ int launch_i8_2sm(const int8_t* q, const int8_t* W, void* out, const float* s_to
 // An INT32 product with too few tiles even at 32 is split along K as well (integer atomics into the zeroed output).
 template <int MODE>
 int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, const float* s_ch, int M, int N, int K,
-             cudaStream_t st) {
+             cudaStream_t st, const u16* bias = nullptr, const u16* lut = nullptr) {
     const int ct = (N + BM - 1) / BM, half = sms() / 2, KB = (K + BK - 1) / BK;
     auto tiles = [&](int bn) { return ct * ((M + bn - 1) / bn); };
     // Large products: the two-SM 256 x 256 tile once every SM pair gets a tile.
-    if (M >= 512 && ((N + 255) / 256) * ((M + 255) / 256) >= half) return launch_i8_2sm<MODE>(q, W, out, s_tok, s_ch, M, N, K, st);
-    if (M > 128 && tiles(256) >= sms() / 4) return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
-    if (M > 64 && tiles(128) >= half) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
-    if (M > 32 && tiles(64) >= half) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
+    if (M >= 512 && ((N + 255) / 256) * ((M + 255) / 256) >= half) return launch_i8_2sm<MODE>(q, W, out, s_tok, s_ch, M, N, K, st, bias, lut);
+    if (M > 128 && tiles(256) >= sms() / 4) return launch_i8<256, 4, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st, bias, lut);
+    if (M > 64 && tiles(128) >= half) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st, bias, lut);
+    if (M > 32 && tiles(64) >= half) return launch_i8<64, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st, bias, lut);
     if (MODE == OUT_I32 && tiles(32) < half) {
         int ks = sms() / tiles(32);
         if (ks > KB / 2) ks = KB / 2;
-        if (ks > 1) return launch_i8<32, 8, MODE, true>(q, W, out, s_tok, s_ch, M, N, K, ks, st);
+        if (ks > 1) return launch_i8<32, 8, MODE, true>(q, W, out, s_tok, s_ch, M, N, K, ks, st, bias, lut);
     }
-    return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st);
+    return launch_i8<32, 8, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st, bias, lut);
 }
 
 // Clusters of `size` CTAs of `kern` (smem bytes each) that can be resident at once (cached per kernel and size).
@@ -907,6 +986,15 @@ int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int
     const int e = check_args(q, W, acc, M, N, K);
     if (e) return e;
     return dispatch<OUT_I32>(q, W, acc, nullptr, nullptr, M, N, K, (cudaStream_t)stream);
+}
+
+int tcq_int8_gemm_bias(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, const uint16_t* bias,
+                       const uint16_t* act_lut, uint16_t* out, int M, int N, int K, void* stream) {
+    const int e = check_args(q, W, out, M, N, K);
+    if (e) return e;
+    if (!s_tok || !s_ch) return TCQ_ERR_ARG;
+    return dispatch<OUT_BF16>(q, W, out, s_tok, s_ch, M, N, K, (cudaStream_t)stream, reinterpret_cast<const u16*>(bias),
+                              reinterpret_cast<const u16*>(act_lut));
 }
 
 int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype, int M,

@@ -77,6 +77,18 @@ __device__ __forceinline__ void tma_load_3d(u32 dst, const CUtensorMap* map, u32
         : "memory");
 }
 
+// Tiled TMA store of a shared-memory box to global memory (bulk-group completion). x is the innermost coordinate; the
+// caller keeps x * element size a multiple of 16 bytes and never starts a store at a negative coordinate.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, u32 src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the thread's committed bulk stores have finished reading their shared-memory sources.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until the thread's committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // cuTensorMapEncodeTiled is a driver entry point; it is resolved through the runtime at first use so that the library
 // does not link libcuda (it loads on machines without a driver, where only the host-side validation is exercised).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,

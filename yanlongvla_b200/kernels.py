@@ -25,7 +25,7 @@ import torch
 from ._lib import DT_BF16, DT_F16, DT_F32, DT_I32, TcqError, check, lib
 
 __all__ = ['quantize', 'pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
-           'gemm_tcq', 'gemm_tcq_tc', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'device_error', 'gelu_table', 'silu_table', 'act_table',
+           'gemm_tcq', 'gemm_tcq_tc', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'int8_gemm_bias', 'device_error', 'gelu_table', 'silu_table', 'act_table',
            'TcqError', 'LAUNCHES']
 
 _DT = {torch.bfloat16: DT_BF16, torch.float32: DT_F32, torch.float16: DT_F16, torch.int32: DT_I32}
@@ -425,6 +425,25 @@ def int8_gemm(q, W, s_tok, s_ch, out=None, out_dtype=torch.bfloat16):
     out = torch.empty(M, N, dtype=out_dtype, device=q.device) if out is None else out
     check(lib.tcq_int8_gemm(_p(q), _p(W), _p(s_tok), _p(s_ch), _p(out), _dt(out, (torch.bfloat16, torch.float32), 'int8_gemm out'),
                             M, N, K, _stream()), 'tcq_int8_gemm')
+    _count('int8_gemm')
+    return out
+
+
+def int8_gemm_bias(q, W, s_tok, s_ch, bias=None, act=None, out=None):
+    """out (M, N) BF16 = act(BF16(int8_gemm(q, W, s_tok, s_ch)) + bias) in one launch (tcq_int8_gemm_bias): the BF16
+    product, the bias as a BF16 tensor add, then the activation table `act` (kernels.act_table: 'gelu' / 'silu') or
+    none, bit-identical to the three PyTorch ops."""
+    _cuda(q, W, s_tok, s_ch, bias, out)
+    M, K = q.shape
+    N = W.shape[0]
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != N or not bias.is_contiguous()):
+        raise TcqError('int8_gemm_bias: bias must be a contiguous (N,) BF16 vector')
+    lut = None if act is None else act_table(act, q.device)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=q.device) if out is None else out
+    if out.dtype != torch.bfloat16 or out.shape != (M, N):
+        raise TcqError('int8_gemm_bias: out must be (M, N) BF16')
+    check(lib.tcq_int8_gemm_bias(_p(q), _p(W), _p(s_tok), _p(s_ch), _p(bias), _p(lut), _p(out), M, N, K, _stream()),
+          'tcq_int8_gemm_bias')
     _count('int8_gemm')
     return out
 

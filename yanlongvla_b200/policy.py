@@ -80,7 +80,11 @@ class W8A8Linear(torch.nn.Module):
         self.W, self.s_ch, self.bias, self.reference = W, s_ch, bias, reference
         self.in_features, self.out_features = W.shape[1], W.shape[0]
 
-    def forward(self, x):
+    def forward(self, x, act=None):
+        """y = act(BF16 product + bias); act None or 'gelu' (tanh approximation). The kernel runtimes add the bias in
+        the GEMM's epilogue (kernels.int8_gemm_bias, the same rounding as the PyTorch add of the reference runtime);
+        the activation stays PyTorch's elementwise op (as a table lookup in the epilogue it costs more than it saves:
+        the 128 KB table does not stay in L1 beside the GEMM's shared-memory stages)."""
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
         if self.reference:                                     # the definition in PyTorch ops (tcq_format.py:119-122)
@@ -89,11 +93,15 @@ class W8A8Linear(torch.nn.Module):
             s = torch.where(amax > 0, amax / torch.full_like(amax, 127.0), torch.ones_like(amax))
             q = torch.clamp(torch.round(h / s), -127, 127).to(torch.int8)
             y = ((K.int_mm(q, self.W).float() * s) * self.s_ch[None, :]).to(torch.bfloat16)
+            if self.bias is not None:
+                y = y + self.bias
+            if act == 'gelu':
+                y = F.gelu(y, approximate='tanh')
         else:
             q, s = K.quantize(x2)
-            y = K.int8_gemm(q, self.W, s, self.s_ch)
-        if self.bias is not None:
-            y = y + self.bias
+            y = K.int8_gemm_bias(q, self.W, s, self.s_ch, bias=self.bias)
+            if act == 'gelu':
+                y = F.gelu(y, approximate='tanh')
         return y.reshape(*shape[:-1], -1)
 
 
@@ -190,7 +198,7 @@ class VitBlock(torch.nn.Module):
         a = self.self_attn
         o = _attention(a.q_proj(h), a.k_proj(h), a.v_proj(h), self.heads)
         x, h = self.layer_norm2(x, a.out_proj(o))
-        return x, self.mlp.fc2(F.gelu(self.mlp.fc1(h), approximate='tanh'))
+        return x, self.mlp.fc2(self.mlp.fc1(h, act='gelu'))
 
 
 class LlmBlock(torch.nn.Module):
@@ -392,7 +400,7 @@ def synthetic_w8a8(model, device, seed=1, reference=False):
             continue
         W = torch.randint(-127, 128, (m.out_features, m.in_features), dtype=torch.int8, device=device, generator=g)
         s_ch = torch.full((m.out_features,), 1.0 / (73.3 * math.sqrt(m.in_features)), device=device)
-        bias = torch.zeros(m.out_features, dtype=torch.bfloat16, device=device) if m.has_bias else None
+        bias = (torch.randn(m.out_features, device=device, generator=g) * 0.02).bfloat16() if m.has_bias else None
         modules.set_submodule(model, name, W8A8Linear(W, s_ch, bias, reference=reference))
 
 
