@@ -481,6 +481,14 @@ int rows_ch(int M, int K, int per_sm) {
 constexpr int kLightPerSm = 1024;   // row kernels of few registers (pre, rotate)
 constexpr int kHeavyPerSm = 512;    // row kernels with the epilogue's operands in registers (post, middles, chain)
 
+// Threads per row of the heavy row kernels (80-96 registers a thread: one 512-thread block fills an SM's register
+// file): more rows than SMs get at most 256 threads a row (two chunks a thread on the widest rows), so that two rows
+// share an SM and 160 rows still run as one wave instead of two.
+int heavy_threads(int M, int N, int CH) {
+    const int t = threads_for(N, CH);
+    return M > tcq_sm_count() && t > 256 ? 256 : t;
+}
+
 // f(std::integral_constant<int, CH>{}) for the chunk width ch (4 or 16).
 template <class F>
 int with_ch(int ch, F f) {
@@ -639,7 +647,7 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);
+        const int T = heavy_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
             case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
@@ -715,7 +723,7 @@ static int post_multi(const void* acc, int acc_dtype, const float* s, const floa
     const size_t smem = (size_t)4 * nmax + (st ? cb : 0);
     return with_ch(rows_ch(M * (int)grid.y, nmax, kHeavyPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(nmax, CH);
+        const int T = heavy_threads(M * (int)grid.y, nmax, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_post_multi<TCQ_DT_I32, CH>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
             case TCQ_DT_F32: return launch(k_post_multi<TCQ_DT_F32, CH>, grid, T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (u16*)y0, (u16*)y1, (u16*)y2, M, n0, n1, n2, lda, act0, nmax, st);
@@ -751,7 +759,7 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)6 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);
+        const int T = heavy_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
@@ -777,7 +785,7 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);
+        const int T = heavy_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
