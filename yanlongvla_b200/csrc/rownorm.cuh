@@ -28,8 +28,6 @@ __host__ __device__ inline int norm_threads(int D, int CH = 16) {
 // Chunks of 16 per thread: one up to 8192 wide, kNormMaxChunks above.
 __host__ __device__ inline int norm_nc(int D) { return D <= 8192 ? 1 : kNormMaxChunks; }
 
-__device__ __forceinline__ float bf16_round(float f) { return bf2f(f2bf(f)); }
-
 // h = BF16(x + y) on a chunk, in place in x (FP32 add, one rounding); the packed BF16 words go to hout when given
 // (aligned to 2 CH bytes).
 template <int CH>

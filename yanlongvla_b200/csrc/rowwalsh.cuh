@@ -207,14 +207,6 @@ __device__ __forceinline__ void store_bf16c_any(u16* p, const u32* w) {
     }
 }
 
-// CH finished FP32 values of chunk i0 into the row buffer at swz(i0 + k).
-template <int CH>
-__device__ __forceinline__ void store_f32_swz(float* buf, int i0, const float* v) {
-    float4* b4 = reinterpret_cast<float4*>(buf);
-#pragma unroll
-    for (int q = 0; q < CH / 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-}
-
 // ---------------------------------------------------------------------------------------------------- loaders
 // NB bytes (4, 8 or a multiple of 16) from p, aligned to min(NB, 16), as 32-bit words. G: p is global memory the
 // kernel only reads (__ldg); otherwise p may be in any address space (plain loads).

@@ -39,21 +39,6 @@ TCQ_HD u32 f2bf2(float lo, float hi) {
     return r;
 }
 
-// 16 values as BF16, element k in the low (even k) or high (odd k) half of w[k / 2].
-TCQ_HD void pack_bf16x16(const float* v, u32* w) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) w[k] = f2bf2(v[2 * k], v[2 * k + 1]);
-}
-
-// The 16 packed values back to FP32 (exact).
-TCQ_HD void unpack_bf16w(const u32* w, float* v) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        v[2 * k] = __uint_as_float(w[k] << 16);
-        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-    }
-}
-
 // Two 16-byte stores of 8 packed words (p 16-byte aligned: global or shared).
 TCQ_HD void store16_bf16(u16* p, const u32* w) {
     uint4* u = reinterpret_cast<uint4*>(p);
@@ -118,12 +103,6 @@ static inline FastDiv make_fastdiv(unsigned d) {
 TCQ_HD unsigned fdiv(unsigned n, const FastDiv& f) { return f.d == 1 ? n : __umulhi(n, f.m) >> f.sh; }
 
 // ---------------------------------------------------------------------------------------------------- loads
-TCQ_HD uint4 ldg_nc_v4(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
 // L2 eviction priorities of the decode kernels' two kinds of input: the weight stream is read once per launch (evict
 // first); the per-layer 1 KB decode tables are read by every CTA of every launch of their layer (evict last), so they
 // stay in L2 while the weight streams of the layers in between pass through.
