@@ -211,7 +211,9 @@ int tcq_add_norm(const uint16_t* x, const uint16_t* y, uint16_t* h, uint16_t* ou
  * the model's PyTorch add + norm and kernels.pre, kernels.py:602-628): per token row
  *   y = tcq_post(acc, ...) (acc != NULL; acc_dtype I32 with s / rs, or F32 z already scaled) or y = the BF16 tensor y,
  *   h = BF16(x + y) -> h (h = x without y), n = the norm of tcq_add_norm (same arguments, same arithmetic and order)
- *   -> n when n != NULL, and with su != NULL q / q4 / scale = tcq_pre(BF16(n), su) of the next layer.
+ *   -> n when n != NULL, and with su != NULL q / q4 / scale = tcq_pre(BF16(n), su) of the next layer; with su == NULL
+ *   and q or q4 given, q / q4 / scale = the plain per-token INT8 quantization of BF16(n) (tcq_quantize's arithmetic,
+ *   for a W8A8 next layer).
  * Each stage is bit-identical to the separate entry point. x, y, h, n (M, N) BF16; acc (M, lda) from column col0. */
 int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, const int8_t* sv, const float* bias, int lda,
               int col0, const uint16_t* y, const uint16_t* x, uint16_t* h, uint16_t* n, const void* w, const void* b,

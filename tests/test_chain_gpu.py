@@ -139,3 +139,25 @@ def test_rows_do_not_depend_on_launch_size(K, kind, N):
     for out in (small, large):
         assert torch.equal(out[5], out[1]) and torch.equal(out[6], out[2])
         assert torch.equal(out[7], out[3]) and torch.equal(out[8], out[4])
+
+
+@pytest.mark.parametrize('M,N', [(1, 1152), (128, 1152), (512, 1152), (7, 2048)])
+@pytest.mark.parametrize('add', [False, True])
+def test_chain_quantize_only_equals_addnorm_quantize(K, M, N, add):
+    """No rotation (a W8A8 consumer, the vision tower's layer norms): q / q4 / scale are the plain per-token INT8
+    quantization of the norm output, bit for bit kernels.add_norm followed by kernels.quantize."""
+    g = torch.Generator(device='cuda').manual_seed(M * 7 + N + (1 if add else 0))
+    x = torch.randn(M, N, device='cuda', generator=g).bfloat16()
+    y = torch.randn(M, N, device='cuda', generator=g).bfloat16() if add else None
+    w = (torch.rand(N, device='cuda', generator=g) + 0.5).bfloat16()
+    nb = (torch.randn(N, device='cuda', generator=g) * 0.1).bfloat16()
+    h_ref, n_ref = K.add_norm(x, y, w, nb, 1e-5, 'ln')
+    q_ref, sc_ref = K.quantize(n_ref)
+    q = torch.empty_like(q_ref)
+    q4 = torch.zeros(N // 4, M, dtype=torch.int32, device='cuda')
+    sc = torch.empty_like(sc_ref)
+    kw = {'y': y} if add else {}
+    h, n = K.chain(x, 'ln', w, nb, 1e-5, q=q, q4=q4, scale=sc, want_n=False, **kw)
+    assert n is None and torch.equal(h, h_ref)
+    assert torch.equal(q, q_ref) and torch.equal(sc, sc_ref)
+    assert torch.equal(q4, q_ref.view(M, N // 4, 4).view(torch.int32).view(M, N // 4).t())

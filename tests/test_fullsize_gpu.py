@@ -99,7 +99,7 @@ def test_config4_full_policy_fly_equals_reference(K):
     del ref
     torch.cuda.empty_cache()
     fly, _, info = P.build_policy('cuda', 'fly', c, layers=layers)
-    assert info['chains'] == 2 * (c.llm_layers + c.dit_layers)
+    assert info['chains'] == 2 * (c.llm_layers + c.dit_layers + c.vit_layers)
     with torch.no_grad():
         a = fly(*obs)
     torch.cuda.synchronize()

@@ -31,7 +31,7 @@ def test_policy_runtimes_match_reference(built, runtime):
     P, c, layers, obs, a_ref = built
     model, _, info = P.build_policy('cuda', runtime, c, layers=layers)
     assert info['fused_mlps'] == c.llm_layers + c.dit_layers
-    assert info['chains'] == 2 * (c.llm_layers + c.dit_layers)   # every 2-bit block boundary fused
+    assert info['chains'] == 2 * (c.llm_layers + c.dit_layers + c.vit_layers)   # every block boundary fused
     with torch.no_grad():
         if runtime == 'hybrid':
             modules.decode_chunk(model)

@@ -334,7 +334,23 @@ __global__ void __launch_bounds__(512, 1) k_chain(const void* __restrict__ acc, 
             store_bf16c<CH>(yb + CH * c, wn);
         }
     }
-    if (!su) return;
+    if (!su) {
+        if (!q && !q4) return;
+        // No rotation: the per-token INT8 quantization of BF16(n) itself (the W8A8 layers' quantizer, tcq_quantize's
+        // arithmetic). quantize_store's block maximum synchronizes before any thread reads another's values.
+        float mx = 0.f;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = threadIdx.x + k * blockDim.x;
+            if (c < nch) {
+                float nv[CH];
+                load_bf16c_any<CH>(yb + CH * c, nv);
+                store_chunk<CH>(buf, CH * c, nv, mx);
+            }
+        }
+        quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+        return;
+    }
     __syncthreads();
     float mx = 0.f;
     row_walshc<CH>(buf, N,
@@ -661,7 +677,7 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
               int col0, const uint16_t* y, const uint16_t* x, uint16_t* h, uint16_t* n, const void* w, const void* b,
               int wb_dtype, const uint16_t* mod_scale, const uint16_t* mod_shift, int mod_rows, int ld_mod, float eps,
               int kind, const int8_t* su, int8_t* q, int32_t* q4, float* scale, int ldq, int M, int N, void* stream) {
-    if (!x || (acc && y) || (!n && !su) || (!mod_scale != !mod_shift)) return TCQ_ERR_ARG;
+    if (!x || (acc && y) || (!n && !su && !q && !q4) || (!mod_scale != !mod_shift)) return TCQ_ERR_ARG;
     if (kind != 0 && kind != 1) return TCQ_ERR_ARG;
     if (wb_dtype != TCQ_DT_F32 && wb_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
     if (M <= 0 || !width_ok(N)) return TCQ_ERR_SHAPE;
@@ -672,7 +688,7 @@ int tcq_chain(const void* acc, int acc_dtype, const float* s, const float* rs, c
         if (col0 < 0 || lda < col0 + N) return TCQ_ERR_SHAPE;
         if (!acc_aligned(acc, acc_dtype, lda, col0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
     }
-    if (su && (!scale || (!q && !q4) || (q4 && ldq < M))) return TCQ_ERR_ARG;
+    if ((su || q || q4) && (!scale || (!q && !q4) || (q4 && ldq < M))) return TCQ_ERR_ARG;
     if (mod_scale && (mod_rows <= 0 || ld_mod < N)) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || (y && !tcq_aligned(y, 16)) || (h && !tcq_aligned(h, 16)) || (n && !tcq_aligned(n, 16)) ||
         (su && !tcq_aligned(su, 16)) || (q && !tcq_aligned(q, 16)))

@@ -279,7 +279,8 @@ def chain(x, kind, weight=None, nbias=None, eps=1e-6, *, acc=None, s=None, rs=No
     """Fused post -> residual add -> norm -> pre of one block boundary (tcq_chain). x (M, N) BF16 residual; the add
     takes the post of acc (FP32 z, or INT32 with token scales s and row scales rs; sv / bias of the producing layer,
     its columns from col0) or a BF16 tensor y; the norm is add_norm's (kind, weight, nbias, eps, mod); with su the next
-    layer's rotation + INT8 quantization goes to q and/or q4 (K/4, ldq) words and scale (M,). Returns (h, n): h the
+    layer's rotation + INT8 quantization goes to q and/or q4 (K/4, ldq) words and scale (M,); with q / q4 but no su,
+    the plain per-token quantization of BF16(n) (a W8A8 consumer, kernels.quantize's arithmetic). Returns (h, n): h the
     new residual (x itself without an add), n the BF16 norm output (None when want_n is False)."""
     M, N = x.shape
     if x.dtype != torch.bfloat16 or not x.is_contiguous():
@@ -306,10 +307,11 @@ def chain(x, kind, weight=None, nbias=None, eps=1e-6, *, acc=None, s=None, rs=No
         if ms.dtype != torch.bfloat16 or mh.dtype != torch.bfloat16 or ms.shape[-1] != N or ms.stride(-1) != 1 or ms.stride(0) != mh.stride(0):
             raise TcqError('chain: mod must be BF16 (G, N) views with unit inner stride')
         ld = ms.stride(0)
-    if su is not None and (scale is None or (q is None and q4 is None)):
-        raise TcqError('chain: the pre needs scale and q and/or q4')
+    quant = su is not None or q is not None or q4 is not None
+    if quant and (scale is None or (q is None and q4 is None)):
+        raise TcqError('chain: the quantized output needs scale and q and/or q4')
     h = x if (acc is None and y is None) else (torch.empty_like(x) if h_out is None else h_out)
-    n = torch.empty_like(x) if (want_n or su is None) else None
+    n = torch.empty_like(x) if (want_n or not quant) else None
     _cuda(x, acc, y, h, n, weight, nbias, sv, bias, su, q, q4, scale)
     check(lib.tcq_chain(_p(acc), adt, _p(s), _p(rs), _p(sv), _p(bias), 0 if acc is None else acc.shape[1], int(col0),
                         _p(y), _p(x), None if (acc is None and y is None) else _p(h), _p(n), _p(weight), _p(nbias),

@@ -72,6 +72,13 @@ class LinearSlot(torch.nn.Module):
         raise RuntimeError('quantized Linear slot used before quantize()')
 
 
+class W8Act:
+    """A W8A8 layer's input already quantized per token by the producing norm (kernels.chain with q but no su):
+    q (M, K) int8, s (M,) FP32, shape the activation's shape."""
+    def __init__(self, q, s, shape):
+        self.q, self.s, self.shape = q, s, shape
+
+
 class W8A8Linear(torch.nn.Module):
     """W8A8 Linear of the vision tower: per-token INT8 activations (no rotation), INT8 weights (N, K) with per-channel
     FP32 scales, exact INT32 product, y = BF16(((float)acc * s_tok) * s_ch) + bias."""
@@ -85,6 +92,12 @@ class W8A8Linear(torch.nn.Module):
         the GEMM's epilogue (kernels.int8_gemm_bias, the same rounding as the PyTorch add of the reference runtime);
         the activation stays PyTorch's elementwise op (as a table lookup in the epilogue it costs more than it saves:
         the 128 KB table does not stay in L1 beside the GEMM's shared-memory stages)."""
+        if isinstance(x, W8Act):
+            shape = x.shape
+            y = K.int8_gemm_bias(x.q, self.W, x.s, self.s_ch, bias=self.bias)
+            if act == 'gelu':
+                y = F.gelu(y, approximate='tanh')
+            return y.reshape(*shape[:-1], -1)
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
         if self.reference:                                     # the definition in PyTorch ops (tcq_format.py:119-122)
@@ -103,6 +116,28 @@ class W8A8Linear(torch.nn.Module):
             if act == 'gelu':
                 y = F.gelu(y, approximate='tanh')
         return y.reshape(*shape[:-1], -1)
+
+
+class W8A8Group(torch.nn.Module):
+    """W8A8 layers that read the same input (the vision tower's q / k / v): one GEMM over the concatenated weights,
+    per-channel scales and biases; returns the layers' outputs as column views of its output. Every output element is
+    computed exactly as by the layer alone."""
+    def __init__(self, parts):
+        super().__init__()
+        self.W = torch.cat([m.W for m in parts]).contiguous()
+        self.s_ch = torch.cat([m.s_ch for m in parts]).contiguous()
+        self.bias = torch.cat([m.bias for m in parts]).contiguous() if parts[0].bias is not None else None
+        self.sizes = [m.out_features for m in parts]
+
+    def forward(self, x):
+        shape = x.shape
+        if isinstance(x, W8Act):
+            y = K.int8_gemm_bias(x.q, self.W, x.s, self.s_ch, bias=self.bias)
+        else:
+            q, s = K.quantize(x.reshape(-1, shape[-1]).contiguous())
+            y = K.int8_gemm_bias(q, self.W, s, self.s_ch, bias=self.bias)
+        y = y.view(*shape[:-1], -1)
+        return tuple(torch.split(y, self.sizes, dim=-1))
 
 
 def _attention(q, k, v, heads, kv_heads=None, causal=False):
@@ -132,6 +167,15 @@ def _norm(norm, kind, x, delta, weight, bias, eps, mod=None, mod_rows=1):
     quantization runs in the same kernel and the normed activation is returned as a modules.QAct for that group.
     Returns (x + delta, normed activation)."""
     consumer = getattr(norm, 'consumer', None)
+    if getattr(norm, 'w8_consumer', False) and not isinstance(delta, modules.Deferred) and mod is None:
+        # W8A8 consumers: the norm quantizes its output per token in the same kernel (no rotation)
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        q = torch.empty(x2.shape, dtype=torch.int8, device=x.device)
+        s = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        kw = {} if delta is None else {'y': delta.reshape(x2.shape)}
+        h, _ = K.chain(x2, kind, weight, bias, eps, q=q, scale=s, want_n=False, **kw)
+        return h.view(shape), W8Act(q, s, shape)
     if consumer is None and not isinstance(delta, modules.Deferred):
         return K.add_norm(x, delta, weight, bias, eps, kind, mod=mod, mod_rows=mod_rows)
     shape = x.shape
@@ -196,7 +240,8 @@ class VitBlock(torch.nn.Module):
     def forward(self, x, delta=None):
         x, h = self.layer_norm1(x, delta)
         a = self.self_attn
-        o = _attention(a.q_proj(h), a.k_proj(h), a.v_proj(h), self.heads)
+        qkv = a.qkv(h) if hasattr(a, 'qkv') else (a.q_proj(h), a.k_proj(h), a.v_proj(h))
+        o = _attention(*qkv, self.heads)
         x, h = self.layer_norm2(x, a.out_proj(o))
         return x, self.mlp.fc2(self.mlp.fc1(h, act='gelu'))
 
@@ -454,6 +499,20 @@ def wire_chains(model):
         consume(blk.norm3, blk.ff)
         defer(blk.attn1.o_proj)
         defer(blk.ff)
+    for blk in model.vit:
+        # W8A8 vision blocks: both norms quantize for their consumers, and q / k / v run as one GEMM (their weights
+        # become views of the group's concatenation)
+        a = blk.self_attn
+        if all(isinstance(m, W8A8Linear) for m in (a.q_proj, a.k_proj, a.v_proj, blk.mlp.fc1)):
+            a.qkv = W8A8Group([a.q_proj, a.k_proj, a.v_proj])
+            off = 0
+            for m in (a.q_proj, a.k_proj, a.v_proj):
+                m.W, m.s_ch = a.qkv.W[off:off + m.out_features], a.qkv.s_ch[off:off + m.out_features]
+                if m.bias is not None:
+                    m.bias = a.qkv.bias[off:off + m.out_features]
+                off += m.out_features
+            blk.layer_norm1.w8_consumer = blk.layer_norm2.w8_consumer = True
+            wired += 2
     return wired
 
 
