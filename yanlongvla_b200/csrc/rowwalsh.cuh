@@ -20,19 +20,22 @@ template <int R, class Fin>
 __device__ __forceinline__ void walsh_pass(float* buf, int off, int w, int S, bool last, Fin& fin) {
     const int G = w >> R;
     const float c = wscale(w);
+#pragma unroll 1
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
         const int low = g & (S - 1);
         const int base = off + (((g - low) << R) | low);
+        // S is a multiple of 128 and swz only permutes bits 2..3 by bits 5..6, so swz(base + k S) = swz(base) + k S.
+        float* p = buf + swz(base);
         float v[1 << R];
 #pragma unroll
-        for (int k = 0; k < (1 << R); ++k) v[k] = buf[swz(base + k * S)];
+        for (int k = 0; k < (1 << R); ++k) v[k] = p[k * S];
         bfly<R>(v);
         if (last) {
 #pragma unroll
             for (int k = 0; k < (1 << R); ++k) fin(base + k * S, v[k] * c);
         } else {
 #pragma unroll
-            for (int k = 0; k < (1 << R); ++k) buf[swz(base + k * S)] = v[k];
+            for (int k = 0; k < (1 << R); ++k) p[k * S] = v[k];
         }
     }
 }
@@ -54,51 +57,69 @@ struct ChunkLog {
 // 32 CH are then done. Wider blocks finish with radix-16 passes through shared memory at stride 32 CH (then 16 times
 // that). Threads per row are a multiple of 32, so a warp's chunks are consecutive; blocks are aligned to their width,
 // so a stage never pairs chunks of different blocks. The cross-lane stages are a rolled loop (less code to fetch).
-template <int CH, class Ldc, class Finc, class Fin>
+// A thread with several chunks (rows wider than its block's threads hold at once) loads the inputs of NP of them
+// before transforming any, so that their global-memory round trips overlap instead of following one another. ldc
+// only reads (the same thread's chunks may be rewritten by finc afterwards).
+template <int CH, int NP = (CH == 4 ? 2 : 1), class Ldc, class Finc, class Fin>
 __device__ __forceinline__ void row_walshc(float* buf, int K, Ldc ldc, Finc finc, Fin fin) {
     constexpr int LC = ChunkLog<CH>::value;
     const int nch = K >> LC, lane = threadIdx.x & 31;
-    for (int c0 = threadIdx.x - lane; c0 < nch; c0 += blockDim.x) {        // warp-uniform
-        const int c = c0 + lane;
-        float v[CH];
-        int w = 0;                                                             // width of this chunk's block
-        if (c < nch) {
-            ldc(c, v);
-            bfly<LC>(v);
-            w = block_of(c << LC, K);
-        } else {
-#pragma unroll
-            for (int k = 0; k < CH; ++k) v[k] = 0.f;
-        }
 #pragma unroll 1
-        for (int hc = 1; hc < 32; hc <<= 1) {                                 // stage h = CH hc
-            if (!__any_sync(0xffffffffu, w > CH * hc)) break;
-            const bool act = w > CH * hc;
-            const float sg = (lane & hc) ? -1.f : 1.f;                         // upper lane: partner - own
+    for (int cg = threadIdx.x - lane; cg < nch; cg += NP * blockDim.x) {     // warp-uniform
+        float vv[NP][CH];
 #pragma unroll
-            for (int k = 0; k < CH; ++k) {
-                const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
-                if (act) v[k] = __fmaf_rn(sg, v[k], p);
+        for (int j = 0; j < NP; ++j) {
+            const int c = cg + j * (int)blockDim.x + lane;
+            if (c < nch) {
+                ldc(c, vv[j]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < CH; ++k) vv[j][k] = 0.f;
             }
         }
-        if (c < nch) {
-            const int i0 = c << LC;
-            if (w <= 32 * CH) {
-                const float sc = wscale(w);
 #pragma unroll
-                for (int k = 0; k < CH; ++k) v[k] = v[k] * sc;
-                finc(i0, v);
-            } else {
-                float4* b4 = reinterpret_cast<float4*>(buf);
+        for (int j = 0; j < NP; ++j) {
+            const int c0 = cg + j * (int)blockDim.x;
+            if (c0 >= nch) break;                                              // warp-uniform
+            const int c = c0 + lane;
+            float* v = vv[j];
+            int w = 0;                                                         // width of this chunk's block
+            if (c < nch) {
+                bfly<LC>(v);
+                w = block_of(c << LC, K);
+            }
+#pragma unroll 1
+            for (int hc = 1; hc < 32; hc <<= 1) {                             // stage h = CH hc
+                if (!__any_sync(0xffffffffu, w > CH * hc)) break;
+                const bool act = w > CH * hc;
+                const float sg = (lane & hc) ? -1.f : 1.f;                     // upper lane: partner - own
 #pragma unroll
-                for (int q = 0; q < CH / 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                for (int k = 0; k < CH; ++k) {
+                    const float p = __shfl_xor_sync(0xffffffffu, v[k], hc);
+                    if (act) v[k] = __fmaf_rn(sg, v[k], p);
+                }
+            }
+            if (c < nch) {
+                const int i0 = c << LC;
+                if (w <= 32 * CH) {
+                    const float sc = wscale(w);
+#pragma unroll
+                    for (int k = 0; k < CH; ++k) v[k] = v[k] * sc;
+                    finc(i0, v);
+                } else {
+                    float4* b4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+                    for (int q = 0; q < CH / 4; ++q) b4[swz(i0 + 4 * q) >> 2] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                }
             }
         }
     }
     __syncthreads();
+#pragma unroll 1
     for (int S = 32 * CH;; S <<= 4) {
         bool work = false;
         int off = 0;
+#pragma unroll 1
         for (int rem = K; rem;) {
             const int w = 1 << (31 - __clz(rem));
             if (w > S) {
@@ -167,6 +188,7 @@ __device__ __forceinline__ void quantize_store(const float* buf, float mx, float
     const float s = mx > 0.f ? mx / 127.f : 1.f;
     if (threadIdx.x == 0) scale[tok] = s;
     const float4* b4 = reinterpret_cast<const float4*>(buf);
+#pragma unroll 1
     for (int g = threadIdx.x; g < (K >> 2); g += blockDim.x) {
         const float4 v = b4[swz(4 * g) >> 2];
         const u32 w = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |

@@ -8,6 +8,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "../../include/tcq_b200.h"
 
@@ -53,8 +54,25 @@ TCQ_HD float h2f(u16 h) {
 }
 
 // ---------------------------------------------------------------------------------------------------- Walsh helpers
-// FP32 block scale of a power-of-two width: (float)(1 / sqrt((double)w)) (tcq_format.py:36-41).
-TCQ_HD float wscale(int w) { return (float)(1.0 / sqrt((double)w)); }
+// FP32 block scale of a power-of-two width w = 2^k: (float)(1 / sqrt((double)w)) (tcq_format.py:36-41), built from
+// its bits instead of FP64 arithmetic. Even k: exactly 2^(-k/2). Odd k: sqrt((double)2^k) = 2^((k-1)/2) * RN(sqrt 2)
+// and the quotient and the FP32 rounding scale by the same power of two, so the result is (float)(1 / sqrt(2.0)) =
+// 0x3F3504F3 (the FP32 rounding of 0.70710678...) times 2^(-(k-1)/2): its exponent field lowered by (k - 1) / 2.
+TCQ_HD float wscale(int w) {
+#ifdef __CUDA_ARCH__
+    const int k = 31 - __clz(w);
+#else
+    const int k = 31 - __builtin_clz((unsigned)w);
+#endif
+    const u32 b = (k & 1) ? 0x3F3504F3u - ((u32)(k >> 1) << 23) : (127u - (u32)(k >> 1)) << 23;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(b);
+#else
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+#endif
+}
 
 // R radix-2 stages on 2^R values in registers: stage s pairs slot k with k + 2^s, low slot gets a + b, high slot a - b.
 template <int R>
