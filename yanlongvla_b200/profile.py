@@ -70,12 +70,12 @@ def kernel_classes(graph, warm=3):
 # ----------------------------------------------------------------------------------------------- profiling cases
 # Small, seeded invocations of one kernel each, for a profiler to capture (nothing is timed or checked here):
 #   python -m yanlongvla_b200.profile gemv [--n 4096] [--k 4096] [--tokens 1] [--launches 4]
-#   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--launches 4]
+#   python -m yanlongvla_b200.profile gemm [--m 4096] [--k 2048] [--n 8192] [--out i32|bf16] [--launches 4]
 #   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
 #   python -m yanlongvla_b200.profile chain [--m 17] [--k 1536] [--launches 6]
 #   python -m yanlongvla_b200.profile gemv_tc [--n 1536] [--k 1536] [--tokens 17] [--launches 4]
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
-# kernels.int_mm on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
+# kernels.int_mm (INT32 out) or kernels.int8_gemm (BF16 out with the scale epilogue) on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
 def _case_gemv(n, k, tokens, launches):
     from . import kernels as K
@@ -110,12 +110,19 @@ def _case_gemv_tc(n, k, tokens, launches):
         K.gemm_tcq_tc(bits, t8, q, s, rs, z, k)
 
 
-def _case_gemm(m, k, n, launches):
+def _case_gemm(m, k, n, launches, out_kind='i32'):
     from . import kernels as K
     dev = torch.device('cuda')
     g = torch.Generator(device=dev).manual_seed(12)
     q = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev, generator=g)
     w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+    if out_kind == 'bf16':
+        s_tok = torch.rand(m, device=dev, generator=g) * 1e-2
+        s_ch = torch.rand(n, device=dev, generator=g) * 1e-3
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        for _ in range(launches):
+            K.int8_gemm(q, w, s_tok, s_ch, out=out)
+        return
     out = torch.empty(m, n, dtype=torch.int32, device=dev)
     for _ in range(launches):
         K.int_mm(q, w, out=out)
@@ -164,13 +171,14 @@ def main(argv=None):
     ap.add_argument('--k', type=int, default=None)
     ap.add_argument('--tokens', type=int, default=1)
     ap.add_argument('--launches', type=int, default=4)
+    ap.add_argument('--out', choices=['i32', 'bf16'], default='i32', help='gemm case: INT32 or BF16 (scaled) output')
     a = ap.parse_args(argv)
     if a.case == 'gemv':
         _case_gemv(a.n or 4096, a.k or 4096, a.tokens, a.launches)
     elif a.case == 'gemv_tc':
         _case_gemv_tc(a.n or 1536, a.k or 1536, a.tokens, a.launches)
     elif a.case == 'gemm':
-        _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches)
+        _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches, a.out)
     elif a.case == 'chain':
         _case_chain(a.m, a.k or 1536, a.launches)
     else:
