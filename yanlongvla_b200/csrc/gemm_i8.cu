@@ -25,8 +25,6 @@ using namespace tcq;
 
 constexpr int BM = 128;           // channels per tile
 constexpr int BK = 128;           // K bytes per stage
-constexpr int kEpiWarps1 = 8;                // single-SM GEMM: two epilogue warps per TMEM lane quarter
-constexpr int kThreads1 = 64 + 32 * kEpiWarps1;
 
 // Bounded wait that reports through this file's device error flag.
 __device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, volatile int* abort_flag, unsigned long long limit = kWaitNs) {
@@ -76,21 +74,25 @@ __device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&v)[32]) {
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_BF16 = 2 };
 
-constexpr int kEpiStageBytes = 32 * 32 * 4;   // per epilogue warp: one 32-token x 32-channel box of the output
+// Epilogue warps of the GEMMs (warps 2 .., after the TMA and MMA warps): sixteen for BF16 output, four per TMEM lane
+// quarter (its scaling and paired conversion are the heaviest epilogue work; a single-tile CTA waits for all of it),
+// eight otherwise. Each warp stages one 32-token x 32-channel box of the output.
+constexpr int epi_warps(int mode) { return mode == OUT_BF16 ? 16 : 8; }
+constexpr int epi_threads(int mode) { return 64 + 32 * epi_warps(mode); }
+constexpr int epi_box_bytes(int mode) { return mode == OUT_BF16 ? 32 * 32 * 2 : 32 * 32 * 4; }
 
 // One epilogue step of a warp: TMEM column group v of its lane's channel ch0 + lane, tokens t0 .. t0 + 31, into the
 // output: INT32 as is, or z = ((float)acc * s_tok[t]) * s_ch[n] as FP32 or BF16 (BF16 then + bias as a BF16 tensor add,
-// then the activation table: the PyTorch ops of a biased layer, bit for bit). The token scales come in one coalesced
-// load and go round the warp by shuffles. tma: the values are written token-major into the warp's staging box and one
+// then the activation table: the PyTorch ops of a biased layer, bit for bit). stv: lane l's token scale s_tok[t0 + l]
+// (0 past M), loaded by the caller before it waits for the accumulator (the load's latency hides behind the MMAs);
+// the scales go round the warp by shuffles. tma: the values are written token-major into the warp's staging box and one
 // TMA store writes the box (rows past M, columns past N clipped by the tensor map), instead of 32 two- or four-byte
 // stores per lane with stride N.
 template <int MODE, bool SPLIT>
 __device__ __forceinline__ void epi_chunk(const u32 (&v)[32], int lane, int ch0, int t0, int M, int N, float sc, float bb,
-                                          const float* __restrict__ s_tok, const u16* __restrict__ bias,
-                                          const u16* __restrict__ lut, void* __restrict__ out, uint8_t* stage,
-                                          const CUtensorMap* tmO, bool tma) {
+                                          float stv, const u16* __restrict__ bias, const u16* __restrict__ lut,
+                                          void* __restrict__ out, uint8_t* stage, const CUtensorMap* tmO, bool tma) {
     const int ch = ch0 + lane;
-    const float stv = MODE != OUT_I32 && t0 + lane < M ? s_tok[t0 + lane] : 0.f;
     auto value = [&](int j, float st) -> u32 {
         if (MODE == OUT_I32) return v[j];
         const float z = ((float)(int)v[j] * st) * sc;
@@ -152,7 +154,7 @@ __device__ __forceinline__ void epi_chunk(const u32 (&v)[32], int lane, int ch0,
 }
 
 template <int BN, int STAGES, int MODE, bool SPLIT>
-__global__ void __launch_bounds__(kThreads1, 1)
+__global__ void __launch_bounds__(epi_threads(MODE), 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
           const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K, int ks,
           const u16* __restrict__ bias, const u16* __restrict__ lut, const __grid_constant__ CUtensorMap tmO, int tma) {
@@ -164,7 +166,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
     uint8_t* sE = sB + STAGES * B_BYTES;                     // epilogue staging boxes (warps 2..9)
-    u64* bars = reinterpret_cast<u64*>(sE + kEpiWarps1 * kEpiStageBytes);
+    u64* bars = reinterpret_cast<u64*>(sE + epi_warps(MODE) * epi_box_bytes(MODE));
     u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * STAGES + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
@@ -182,7 +184,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 32 * kEpiWarps1);    // every thread of the epilogue warps
+            mbar_init(tempty0 + 8 * a, 32 * epi_warps(MODE));    // every thread of the epilogue warps
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -263,24 +265,38 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUten
         }
     } else {
         const int q = warp & 3;                  // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;        // its share of the tile's 32-token column groups: every other one
+        constexpr int GW = epi_warps(MODE) / 4;  // warps per lane quarter: each takes every GW-th 32-token column group
+        const int grp = (warp - 2) >> 2;
+        constexpr int NCW = (BN / 32 + GW - 1) / GW;   // column groups of a warp, at most
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const int a = it & 1;
             const u32 aph = (it >> 1) & 1;
-            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
-            tc_fence_after();
+            // The tile's channel and token scales first: their loads complete while the MMAs still run.
             const int tt = tile / ks, tn = tt % tiles_n, tm = tt / tiles_n;
             const int ch0 = tn * BM + 32 * q, ch = ch0 + lane, m0 = tm * BN;
             const bool chok = ch < N;
             const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
             const float bb = (MODE == OUT_BF16 && bias && chok) ? bf2f(bias[ch]) : 0.f;
+            float stv[NCW];
+#pragma unroll
+            for (int i = 0; i < NCW; ++i) {
+                const int t = m0 + 32 * (grp + GW * i) + lane;
+                stv[i] = MODE != OUT_I32 && grp + GW * i < BN / 32 && t < M ? s_tok[t] : 0.f;
+            }
+            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
+            tc_fence_after();
 #pragma unroll 1
-            for (int c = half; c < BN / 32; c += 2) {
+            for (int i = 0; i < NCW; ++i) {
+                const int c = grp + GW * i;
+                if (c >= BN / 32) break;
+                float st = stv[0];
+#pragma unroll
+                for (int j = 1; j < NCW; ++j) st = i == j ? stv[j] : st;
                 u32 v[32];
                 tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * BN + 32 * c), v);
-                epi_chunk<MODE, SPLIT>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, s_tok, bias, lut, out,
-                                       sE + (warp - 2) * kEpiStageBytes, &tmO, tma != 0);
+                epi_chunk<MODE, SPLIT>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, st, bias, lut, out,
+                                       sE + (warp - 2) * epi_box_bytes(MODE), &tmO, tma != 0);
             }
             tc_fence_before();
             mbar_arrive(tempty0 + 8 * a);
@@ -321,8 +337,6 @@ __global__ void k_wait_expiry(unsigned long long limit_ns) {
 // (tokens) from its own TMEM and releases the buffer on the leader's barrier with a remote arrive.
 constexpr int kStages2 = 6;
 constexpr int kHalf = 128;                                   // channels / tokens per CTA of the pair
-constexpr int kEpiWarps2 = 8;                                // epilogue warps: two per TMEM lane quarter, each half the tokens
-constexpr int kThreads2 = 64 + 32 * kEpiWarps2;
 
 __device__ __forceinline__ u32 cluster_rank() {
     u32 r;
@@ -367,7 +381,7 @@ constexpr u32 idesc_i8_pair() {
 }
 
 template <int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(epi_threads(MODE), 1)
 k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ, void* __restrict__ out,
               const float* __restrict__ s_tok, const float* __restrict__ s_ch, int M, int N, int K,
               const u16* __restrict__ bias, const u16* __restrict__ lut, const __grid_constant__ CUtensorMap tmO, int tma) {
@@ -379,7 +393,7 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     uint8_t* sA = smem;
     uint8_t* sB = smem + kStages2 * A_BYTES;
     uint8_t* sE = sB + kStages2 * B_BYTES;                   // epilogue staging boxes (warps 2..9)
-    u64* bars = reinterpret_cast<u64*>(sE + kEpiWarps2 * kEpiStageBytes);
+    u64* bars = reinterpret_cast<u64*>(sE + epi_warps(MODE) * epi_box_bytes(MODE));
     u32* tmem_slot = reinterpret_cast<u32*>(bars + 2 * kStages2 + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const u32 full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages2), tfull0 = smem_u32(bars + 2 * kStages2),
@@ -398,7 +412,7 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);                    // the leader's MMA commit (multicast)
-            mbar_init(tempty0 + 8 * a, 2 * kEpiWarps2);     // the epilogue warps of both CTAs (used in the leader)
+            mbar_init(tempty0 + 8 * a, 2 * epi_warps(MODE));     // the epilogue warps of both CTAs (used in the leader)
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -468,25 +482,37 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
         }
     } else {
         const int q = warp & 3;                              // TMEM lane quarter this warp may access
-        const int c0 = ((warp - 2) >> 2) * (256 / 32 / 2);   // its half of the tile's 32-token column groups
+        constexpr int NCW = 256 / 32 / (epi_warps(MODE) / 4);   // 32-token column groups of a warp
+        const int c0 = ((warp - 2) >> 2) * NCW;              // its share of the tile's column groups
         const u32 tempty_leader = map_to_rank(tempty0, 0);
         int it = 0;
         for (int tile = pair; tile < tiles; tile += pairs, ++it) {
             const int a = it & 1;
             const u32 aph = (it >> 1) & 1;
-            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
-            tc_fence_after();
+            // The tile's channel and token scales first: their loads complete while the MMAs still run.
             const int tn = tile % tiles_n, tm = tile / tiles_n;
             const int ch0 = tn * 256 + (int)rank * kHalf + 32 * q, ch = ch0 + lane, m0 = tm * 256;
             const bool chok = ch < N;
             const float sc = (MODE != OUT_I32 && chok) ? s_ch[ch] : 0.f;
             const float bb = (MODE == OUT_BF16 && bias && chok) ? bf2f(bias[ch]) : 0.f;
+            float stv[NCW];
+#pragma unroll
+            for (int i = 0; i < NCW; ++i) {
+                const int t = m0 + 32 * (c0 + i) + lane;
+                stv[i] = MODE != OUT_I32 && t < M ? s_tok[t] : 0.f;
+            }
+            if (!mbar_wait(tfull0 + 8 * a, aph, abort_flag)) break;
+            tc_fence_after();
 #pragma unroll 1
-            for (int c = c0; c < c0 + 256 / 32 / 2; ++c) {
+            for (int i = 0; i < NCW; ++i) {
+                const int c = c0 + i;
+                float st = stv[0];
+#pragma unroll
+                for (int j = 1; j < NCW; ++j) st = i == j ? stv[j] : st;
                 u32 v[32];
                 tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(a * 256 + 32 * c), v);
-                epi_chunk<MODE, false>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, s_tok, bias, lut, out,
-                                       sE + (warp - 2) * kEpiStageBytes, &tmO, tma != 0);
+                epi_chunk<MODE, false>(v, lane, ch0, m0 + 32 * c, M, N, sc, bb, st, bias, lut, out,
+                                       sE + (warp - 2) * epi_box_bytes(MODE), &tmO, tma != 0);
             }
             tc_fence_before();
             __syncwarp();
@@ -824,14 +850,14 @@ int launch_i8(const int8_t* q, const int8_t* W, void* out, const float* s_tok, c
     CUtensorMap tmO = {};
     const int tma = !SPLIT && make_out_map(&tmO, out, M, N, MODE) ? 1 : 0;
     auto kern = k_gemm_i8<BN, STAGES, MODE, SPLIT>;
-    const int smem = 1024 + STAGES * (BM + BN) * BK + kEpiWarps1 * kEpiStageBytes + (2 * STAGES + 4) * 8 + 16;
+    const int smem = 1024 + STAGES * (BM + BN) * BK + epi_warps(MODE) * epi_box_bytes(MODE) + (2 * STAGES + 4) * 8 + 16;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
     if (ks > 1 && cudaMemsetAsync(out, 0, (size_t)M * N * sizeof(int), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
     const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN) * ks;
     const int grid = tiles < sms() ? tiles : sms();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads1);
+    cfg.blockDim = dim3(epi_threads(MODE));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -851,14 +877,14 @@ int launch_i8_2sm(const int8_t* q, const int8_t* W, void* out, const float* s_to
     CUtensorMap tmO = {};
     const int tma = make_out_map(&tmO, out, M, N, MODE) ? 1 : 0;
     auto kern = k_gemm_i8_2sm<MODE>;
-    const int smem = 1024 + kStages2 * 2 * kHalf * BK + kEpiWarps2 * kEpiStageBytes + (2 * kStages2 + 4) * 8 + 16;
+    const int smem = 1024 + kStages2 * 2 * kHalf * BK + epi_warps(MODE) * epi_box_bytes(MODE) + (2 * kStages2 + 4) * 8 + 16;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
     const int tiles = ((N + 255) / 256) * ((M + 255) / 256);
     int pairs = sms() / 2;
     if (pairs > tiles) pairs = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(kThreads2);
+    cfg.blockDim = dim3(epi_threads(MODE));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
