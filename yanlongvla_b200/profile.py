@@ -17,6 +17,7 @@ CLASSES = [
     ('INT8 GEMM (tcgen05)', r'k_gemm_i8'),
     ('INT8-resident GEMV', r'k_gemm_w8'),
     ('rotate + quantize', r'k_pre|k_quant'),
+    ('post + add + norm + pre chain', r'k_chain'),
     ('scale + rotate', r'k_post'),
     ('MLP middles', r'k_mid'),
     ('attention', r'flash|fmha|attention|softmax|sdpa'),
@@ -50,14 +51,15 @@ def kernel_classes(graph, warm=3):
         cls = next(c for c, pat in CLASSES if re.search(pat, e.name))
         by[cls] += dur
         launches[cls] += 1
-        top[e.name[:90]] += dur
+        name = e.name.replace('(anonymous namespace)::', '')[:90]
+        top[name] += dur
         # Kernels launched early by programmatic dependent launch wait for their predecessor inside their own time
         # range, so a kernel's share of the critical path is the time from the previous kernel's end to its own end.
         t0, t1 = e.time_range.start, e.time_range.end
         x = (t1 - max(t0, prev_end if prev_end is not None else t0)) / 1000
         if x > 0:
             excl[cls] += x
-            excl_top[e.name[:90]] += x
+            excl_top[name] += x
         prev_end = t1 if prev_end is None else max(prev_end, t1)
     total = sum(by.values())
     return dict(wall_ms=wall, kernel_ms=total, gaps_ms=max(wall - sum(excl.values()), 0.0), launches=sum(launches.values()),
@@ -74,6 +76,7 @@ def kernel_classes(graph, warm=3):
 #   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
 #   python -m yanlongvla_b200.profile chain [--m 17] [--k 1536] [--launches 6]
 #   python -m yanlongvla_b200.profile gemv_tc [--n 1536] [--k 1536] [--tokens 17] [--launches 4]
+#   python -m yanlongvla_b200.profile policy [--tokens 1]    (kernel_classes of one chunk-graph replay, as JSON)
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
 # kernels.int_mm (INT32 out) or kernels.int8_gemm (BF16 out with the scale epilogue) on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
@@ -162,10 +165,29 @@ def _case_chain(m, n, launches):
         K.chain(x, 'rms', w, None, 1e-6, acc=z, sv=sv, su=su, q=q, scale=s, want_n=False)
 
 
+def _case_policy(batch):
+    """kernel_classes of one CUDA-graph replay of the fly policy's action chunk for `batch` observations."""
+    import json
+    from . import policy as P
+    c = P.PolicyConfig()
+    model, _, _ = P.build_policy('cuda', 'fly', c)
+    obs = P.synthetic_observations(batch, c)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.no_grad(), torch.cuda.stream(s):
+        for _ in range(2):
+            model(*obs)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(g):
+        model(*obs)
+    print(json.dumps(kernel_classes(g), indent=1))
+
+
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description='one kernel case for a profiler')
-    ap.add_argument('case', choices=['gemv', 'gemv_tc', 'gemm', 'pre', 'rotate', 'chain'])
+    ap.add_argument('case', choices=['gemv', 'gemv_tc', 'gemm', 'pre', 'rotate', 'chain', 'policy'])
     ap.add_argument('--m', type=int, default=4096)
     ap.add_argument('--n', type=int, default=None)
     ap.add_argument('--k', type=int, default=None)
@@ -179,6 +201,8 @@ def main(argv=None):
         _case_gemv_tc(a.n or 1536, a.k or 1536, a.tokens, a.launches)
     elif a.case == 'gemm':
         _case_gemm(a.m, a.k or 2048, a.n or 8192, a.launches, a.out)
+    elif a.case == 'policy':
+        _case_policy(a.tokens)
     elif a.case == 'chain':
         _case_chain(a.m, a.k or 1536, a.launches)
     else:
