@@ -333,15 +333,16 @@ def run_policy(args, rank, world, dist):
 
 
 # ------------------------------------------------------------------------------------------------ CPU reference arm
-def cpu_reference(sample_layers, threads):
+def cpu_reference(sample_layers, threads, min_seconds=0.0, max_layers=64):
     """The reference's CPU path of the metric (numpy restatement of tcq_format.py: windowed trellis read, hash decode,
-    exact INT8 product, scale epilogue) on `sample_layers` config-1 layers. Returns (GB/s, seconds)."""
+    exact INT8 product, scale epilogue) on `sample_layers` config-1 layers, or more (up to `max_layers`) until the
+    timed layers have taken `min_seconds`. Returns (GB/s, seconds, timed layers)."""
     sys.path.insert(0, str(ROOT / 'oracle'))
     import tcq_oracle as O
     rng = np.random.default_rng(0)
     per = layer_bytes(M_N, M_N, TOKENS)
-    t0 = time.perf_counter()
-    for i in range(sample_layers):
+    elapsed, n, i = 0.0, 0, 0
+    while i < sample_layers or (elapsed < min_seconds and i < max_layers):
         bits = rng.integers(0, 1 << 16, size=((M_N // 16) ** 2, 32), dtype=np.uint32).astype(np.uint16)
         tlut = (rng.standard_normal((512, 2)) * 0.968).astype(np.float16)
         rsc = rng.uniform(0.005, 0.03, M_N).astype(np.float16)
@@ -349,14 +350,15 @@ def cpu_reference(sample_layers, threads):
         layer = O.Layer(bits, tlut, rsc, sg, sg)
         q = rng.integers(-127, 128, size=(TOKENS, M_N)).astype(np.int8)
         s = np.ones(TOKENS, dtype=np.float32)
-        if i == 0:
-            t0 = time.perf_counter()                   # the first layer is the warm-up
-            O.gemm_z(q, layer.w8_reference(), s, layer.rs)
-            t0 = time.perf_counter()
-            continue
+        t0 = time.perf_counter()                       # only the layer's decode + product + epilogue is timed
         O.gemm_z(q, layer.w8_reference(), s, layer.rs)
-    dt = time.perf_counter() - t0
-    n = max(sample_layers - 1, 1)
+        d = time.perf_counter() - t0
+        if i > 0:                                      # the first layer is the warm-up
+            elapsed += d
+            n += 1
+        i += 1
+    n = max(n, 1)
+    dt = max(elapsed, 1e-9)
     return per * n / dt / 1e9, dt, n
 
 
@@ -431,7 +433,7 @@ def main():
         out['policy'] = run_policy(args, rank, world, dist)
     if rank == 0:
         if not args.no_cpu_baseline:
-            v, dt, nl = cpu_reference(args.ref_layers + 1, os.cpu_count())
+            v, dt, nl = cpu_reference(args.ref_layers + 1, os.cpu_count(), min_seconds=10.0)
             out['cpu_baseline'] = dict(value=round(v, 6), unit='GB/s', cores=os.cpu_count(), kind='port',
                                        sample='%d config-1 layers (decode + exact product + epilogue), %.1f s' % (nl, dt))
         print(json.dumps(out), file=out_file, flush=True)
