@@ -358,7 +358,7 @@ def test_quantizer_ties_and_tiny_scales(K):
     half-integers): exact halves with s = 1, quotients a rounding away from halves, a denormal scale whose reciprocal
     overflows, and an all-zero row; against the oracle's true division."""
     Kd = 256
-    x = np.zeros((5, Kd), dtype=np.float32)
+    x = np.zeros((6, Kd), dtype=np.float32)
     x[0, :-1] = np.arange(-127, 128, dtype=np.float32)[:Kd - 1] + 0.5
     x[0, -1] = 127.0                                           # amax 127: s = 1, every quotient an exact half
     s1 = np.float32(0.0123)
@@ -367,6 +367,12 @@ def test_quantizer_ties_and_tiny_scales(K):
     r = np.random.default_rng(3)
     x[2] = r.standard_normal(Kd).astype(np.float32) * 7
     x[3] = r.standard_normal(Kd).astype(np.float32) * np.float32(1e-40)   # denormal amax: 1/s overflows
+    # quotients one to four ulps either side of a half-integer (inside and just outside the guard band)
+    s5 = np.float32(0.0371)
+    halves = ((np.arange(Kd - 1) % 254) - 127 + 0.5).astype(np.float32) * s5
+    steps = (np.arange(Kd - 1) % 9 - 4).astype(np.int32)
+    x[5, :-1] = (halves.view(np.int32) + steps).view(np.float32)
+    x[5, -1] = np.float32(127.0) * s5
     qd, sd = K.quantize(t(x))
     qo, so = O.quantize_tokens(x)
     assert np.array_equal(n(qd), qo) and np.array_equal(n(sd), so[:, 0])

@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_
         for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(v[k]));
     }
     mx = block_max(mx, red);
-    const float s = mx > 0.f ? mx / 127.f : 1.f;
+    const float s = mx > 0.f ? mx / 127.f : 1.f, rs = 1.f / s;
     if (threadIdx.x == 0) scale[tok] = s;
     for (int c = threadIdx.x; c < (K >> 4); c += blockDim.x) {
         float v[16];
@@ -474,8 +474,8 @@ __global__ void __launch_bounds__(256) k_quant(const void* __restrict__ x, int8_
         u32 w[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g)
-            w[g] = (u32)(q8(v[4 * g], s) & 0xff) | ((u32)(q8(v[4 * g + 1], s) & 0xff) << 8) | ((u32)(q8(v[4 * g + 2], s) & 0xff) << 16) |
-                   ((u32)(q8(v[4 * g + 3], s) & 0xff) << 24);
+            w[g] = (u32)(q8(v[4 * g], s, rs) & 0xff) | ((u32)(q8(v[4 * g + 1], s, rs) & 0xff) << 8) |
+                   ((u32)(q8(v[4 * g + 2], s, rs) & 0xff) << 16) | ((u32)(q8(v[4 * g + 3], s, rs) & 0xff) << 24);
         *reinterpret_cast<uint4*>(q + (size_t)tok * K + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }

@@ -175,8 +175,17 @@ __device__ __forceinline__ float block_max(float mx, float* red) {
 
 // Per-token INT8 quantizer (tcq_format.py:119-122; kernels.py:164-184): s = amax / 127 (IEEE division, 1 when
 // amax = 0), q = clamp(rint(v / s), -127, 127). q (M, K) row-major and/or q4 (K/4, ldq) words, token = column.
-__device__ __forceinline__ int q8(float v, float s) {
-    float r = rintf(v / s);
+//
+// rint(v / s) without a division per element, by a guard band around the rounding boundaries: with rs = 1 / s
+// (IEEE, once per row) the product a = v * rs is within |v / s| * 2^-23 (two roundings of 2^-24) of the true
+// quotient, i.e. within 1.52e-5 for |v / s| <= 127.5. When a lies more than 3.1e-5 from the nearest half-integer,
+// the quotient lies on the same side of it (more than 1.52e-5 away), so rint(a) = rint(v / s); otherwise -- and for
+// NaN, infinities and an overflowing reciprocal, where the test is false -- the quotient is computed by division.
+// Either way the result is rint of the correctly rounded quotient, bit for bit.
+__device__ __forceinline__ int q8(float v, float s, float rs) {
+    const float a = v * rs;
+    float r = rintf(a);
+    if (!(fabsf(fabsf(a - r) - 0.5f) > 3.1e-5f)) r = rintf(v / s);
     r = fminf(fmaxf(r, -127.f), 127.f);
     return (int)r;
 }
@@ -185,14 +194,14 @@ __device__ __forceinline__ int q8(float v, float s) {
 __device__ __forceinline__ void quantize_store(const float* buf, float mx, float* red, int8_t* q, int* q4, float* scale,
                                                int tok, int K, int ldq) {
     mx = block_max(mx, red);
-    const float s = mx > 0.f ? mx / 127.f : 1.f;
+    const float s = mx > 0.f ? mx / 127.f : 1.f, rs = 1.f / s;
     if (threadIdx.x == 0) scale[tok] = s;
     const float4* b4 = reinterpret_cast<const float4*>(buf);
 #pragma unroll 1
     for (int g = threadIdx.x; g < (K >> 2); g += blockDim.x) {
         const float4 v = b4[swz(4 * g) >> 2];
-        const u32 w = (u32)(q8(v.x, s) & 0xff) | ((u32)(q8(v.y, s) & 0xff) << 8) | ((u32)(q8(v.z, s) & 0xff) << 16) |
-                      ((u32)(q8(v.w, s) & 0xff) << 24);
+        const u32 w = (u32)(q8(v.x, s, rs) & 0xff) | ((u32)(q8(v.y, s, rs) & 0xff) << 8) | ((u32)(q8(v.z, s, rs) & 0xff) << 16) |
+                      ((u32)(q8(v.w, s, rs) & 0xff) << 24);
         if (q) reinterpret_cast<u32*>(q + (size_t)tok * K)[g] = w;
         if (q4) q4[(size_t)g * ldq + tok] = (int)w;
     }
