@@ -6,12 +6,16 @@
  *
  * Conventions (all entry points):
  *   - every buffer is a device pointer allocated and owned by the caller; the library allocates nothing and keeps no
- *     per-call state, so calls can be captured in a CUDA graph;
+ *     per-call state, so calls can be captured in a CUDA graph. The one exception is tcq_gemm_tcq_noalloc: it keeps
+ *     its scratch in one fixed array inside the library that every call on a device shares (calls that overlap on
+ *     the GPU race on it), and its first call on a device, which looks up that array's address, must come before
+ *     any stream capture;
  *   - `stream` is a cudaStream_t (NULL = the legacy default stream);
  *   - optional outputs / inputs may be NULL where stated (the reference passes None for them, cuda_rt.py:90-91);
  *   - BF16 values are passed as uint16_t bit patterns; dtype codes are TCQ_DT_*;
  *   - the return value is a tcq_status: 0 on success; shapes and alignment are validated on the host before any
- *     launch, so a non-zero status means nothing was launched (TCQ_ERR_LAUNCH: the launch itself failed).
+ *     launch, so a non-zero status means nothing was launched (TCQ_ERR_LAUNCH: the launch itself failed; for
+ *     tcq_gemm_tcq_noalloc a clear of its own scratch array may already be queued on the stream then).
  */
 #ifndef TCQ_B200_H
 #define TCQ_B200_H

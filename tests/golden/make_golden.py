@@ -1,9 +1,10 @@
 """Generate the golden fixtures by running the reference's own PyTorch definition on CPU.
 
-    python tests/golden/make_golden.py [path/to/reference/deploy/tcq_kernels]
+    python tests/golden/make_golden.py path/to/reference/deploy/tcq_kernels
+    TCQ_REF_ROOT=path/to/reference/deploy/tcq_kernels python tests/golden/make_golden.py
 
-Imports `tcq_format.py` from the reference checkout (read-only; default: $TCQ_REF_ROOT or
-/root/reference/deploy/tcq_kernels), feeds it the seeded inputs of `cases.py`, and writes
+Imports `tcq_format.py` from the reference checkout (read-only; its directory is the first argument, or the
+TCQ_REF_ROOT environment variable; one of them is required), feeds it the seeded inputs of `cases.py`, and writes
 `golden.npz` (small outputs in full) and `golden_sha256.json` (SHA-256 of the exact bytes of every output,
 large ones included). The fixtures, not the reference, travel with the repository: the tests never import it.
 """
@@ -36,7 +37,9 @@ def bf16_np(t):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('TCQ_REF_ROOT', '/root/reference/deploy/tcq_kernels')
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('TCQ_REF_ROOT')
+    if not ref_root:
+        raise SystemExit('make_golden.py: give the reference directory deploy/tcq_kernels as the first argument or in TCQ_REF_ROOT')
     sys.dont_write_bytecode = True
     sys.path.insert(0, ref_root)
     import tcq_format as F                            # the reference definition (read-only import)

@@ -8,7 +8,9 @@ size-independent properties plus oracle checks on sampled rows.
   INT8 GEMM and the same FP32 epilogue, bit for bit (two independent paths, each pinned to the oracle at small sizes).
 - config 2 (rotation), T = 4096, D up to 16384: sampled rows equal the oracle's block Walsh bit for bit, and the
   inverse undoes the forward to FP32 rounding.
-- config 4: the full-size policy (27 / 24 / 16 layers) in the fly runtime equals the reference runtime bit for bit."""
+- config 4: in the full-size policy (27 / 24 / 16 layers) every quantized layer equals the PyTorch-ops definition bit
+  for bit on its in-policy input, and the fly runtime's action chunk is within the task's tolerance of the
+  reference runtime's."""
 import numpy as np
 import pytest
 import torch
@@ -89,18 +91,30 @@ def test_config2_full_rotation(K, D):
     assert err <= 1e-5 * max(1.0, x.float().abs().max().item())
 
 
-def test_config4_full_policy_fly_equals_reference(K):
+def test_config4_full_policy_every_layer_and_chunk(K):
+    """Config 4 at full depth, B = 1: all 442 quantized layers (280 W2A8, 162 W8A8) reproduce the definition's
+    intermediates bit for bit on the inputs they receive in the reference-runtime policy; three of the decodes are
+    also checked against the CPU oracle; the fly chunk is within the task's tolerance of the reference chunk."""
+    import policy_parity as PP
     from yanlongvla_b200 import policy as P
     c = P.PolicyConfig()
     ref, layers, _ = P.build_policy('cuda', 'reference', c)
     obs = P.synthetic_observations(1, c)
-    with torch.no_grad():
-        a_ref = ref(*obs)
-    del ref
+    seen, a_ref = PP.capture_inputs(ref, obs)
+    assert len(seen) == 442
+    rec = PP.layer_records(seen, layers)
+    assert not PP.failures(rec), PP.failures(rec)
+    assert sum(r['kind'] == 'w2a8' for r in rec.values()) == 280
+    for name in ('llm.5.mlp.down_proj', 'dit.3.attn1.q_proj', 'dit.0.adaln'):
+        L = layers[name]
+        ref_layer = O.Layer(n(L.bits).view(np.uint16), n(L.tlut), n(L.row_scale), n(L.su), n(L.sv))
+        assert np.array_equal(n(seen[name][0].w8), ref_layer.w8_reference()), name
+    del seen, ref
     torch.cuda.empty_cache()
     fly, _, info = P.build_policy('cuda', 'fly', c, layers=layers)
     assert info['chains'] == 2 * (c.llm_layers + c.dit_layers + c.vit_layers)
     with torch.no_grad():
         a = fly(*obs)
     torch.cuda.synchronize()
-    assert torch.isfinite(a).all() and torch.equal(a, a_ref)
+    ok, max_rel, cos = PP.within_tolerance(a, a_ref)
+    assert torch.isfinite(a).all() and ok, f'max-abs / RMS {max_rel.tolist()}, cosine {cos.tolist()}'

@@ -1,34 +1,53 @@
-"""The GR00T-style quantized policy: every kernel runtime reproduces the reference runtime (the
-W2A8 / W8A8 definition in PyTorch ops) bit for bit on whole action chunks, and single layers inside the policy match
-the CPU oracle on the inputs they see there."""
-import numpy as np
+"""The GR00T-style quantized policy (BASELINE configs 4 and 5) at reduced depth, against its 'reference' runtime: the
+W2A8 / W8A8 definition with norms and rotary embedding in PyTorch ops (`yanlongvla_b200.definition`), which runs
+nothing of the kernel library.
+
+  * every quantized layer, on the input it receives inside the reference policy, reproduces the definition's
+    intermediates bit for bit through the kernels (tests/policy_parity.py; the reference's parity.py:22-73);
+  * whole action chunks of every kernel runtime are within the task's tolerance of the reference chunk, per
+    observation (max-abs <= 1e-2 x RMS, cosine >= 0.9995), at B = 1 and B = 8: the norms' row sums run in a
+    different order in the kernels, so chunks agree to that tolerance rather than bit for bit;
+  * the kernel runtimes agree with one another bit for bit, and the fused block-boundary chains equal the separate
+    post / add-norm / pre kernels bit for bit.
+"""
 import pytest
 import torch
 
-import tcq_oracle as O
-from gpu_util import n
+import policy_parity as PP
 
 pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope='module')
-def built():
+def small():
     if not torch.cuda.is_available():
         pytest.skip('no CUDA device')
     from yanlongvla_b200 import policy as P
-    c = P.PolicyConfig(vit_layers=4, llm_layers=4, dit_layers=4)
-    ref, layers, _ = P.build_policy('cuda', 'reference', c)
-    obs = P.synthetic_observations(2, c)
+    c = P.PolicyConfig(vit_layers=2, llm_layers=2, dit_layers=2)
+    ref, layers, info = P.build_policy('cuda', 'reference', c)
+    return P, c, ref, layers, info
+
+
+@pytest.mark.parametrize('B', [1, 8])
+def test_every_layer_matches_definition(small, B):
+    P, c, ref, layers, _ = small
+    obs = P.synthetic_observations(B, c, seed=10 + B)
+    seen, _ = PP.capture_inputs(ref, obs)
+    assert len(seen) == 6 * c.vit_layers + 7 * (c.llm_layers + c.dit_layers)
+    rec = PP.layer_records(seen, layers)
+    assert not PP.failures(rec), PP.failures(rec)
+    kinds = {(r['kind'], r['tokens']) for r in rec.values()}
+    assert ('w2a8', B * c.prefix_tokens) in kinds and ('w2a8', B * (c.chunk + 1)) in kinds and ('w2a8', B) in kinds
+
+
+@pytest.mark.parametrize('B', [1, 8])
+@pytest.mark.parametrize('runtime', ['fly', 'resident', 'hybrid'])
+def test_chunk_within_tolerance(small, runtime, B):
+    from yanlongvla_b200 import modules
+    P, c, ref, layers, _ = small
+    obs = P.synthetic_observations(B, c, seed=20 + B)
     with torch.no_grad():
         a_ref = ref(*obs)
-    torch.cuda.synchronize()
-    return P, c, layers, obs, a_ref
-
-
-@pytest.mark.parametrize('runtime', ['fly', 'resident', 'hybrid'])
-def test_policy_runtimes_match_reference(built, runtime):
-    from yanlongvla_b200 import modules
-    P, c, layers, obs, a_ref = built
     model, _, info = P.build_policy('cuda', runtime, c, layers=layers)
     assert info['fused_mlps'] == c.llm_layers + c.dit_layers
     assert info['chains'] == 2 * (c.llm_layers + c.dit_layers + c.vit_layers)   # every block boundary fused
@@ -38,35 +57,29 @@ def test_policy_runtimes_match_reference(built, runtime):
         a = model(*obs)
     torch.cuda.synchronize()
     assert torch.isfinite(a).all()
-    assert torch.equal(a, a_ref), f'max |da| = {float((a - a_ref).abs().max())}'
+    ok, max_rel, cos = PP.within_tolerance(a, a_ref)
+    assert ok, f'max-abs / RMS {max_rel.tolist()}, cosine {cos.tolist()}'
 
 
-def test_policy_layers_match_oracle(built):
-    """Hook two quantized layers (LLM q/k/v group member, DiT AdaLN at M = batch) and check them against the oracle."""
+def test_kernel_runtimes_agree_and_chains_equal_unfused(small):
     from yanlongvla_b200 import modules
-    P, c, layers, obs, _ = built
-    modules.FUSE['chain'] = False                  # the hooks read each layer's input as a tensor
+    P, c, _, layers, _ = small
+    obs = P.synthetic_observations(3, c, seed=30)
+    outs = {}
+    for runtime in ('fly', 'resident', 'hybrid'):
+        model, _, _ = P.build_policy('cuda', runtime, c, layers=layers)
+        with torch.no_grad():
+            if runtime == 'hybrid':
+                modules.decode_chunk(model)
+            outs[runtime] = model(*obs)
+    modules.FUSE['chain'] = False
     try:
         model, _, info = P.build_policy('cuda', 'fly', c, layers=layers)
     finally:
         modules.FUSE['chain'] = True
     assert info['chains'] == 0
-    seen = {}
-
-    def hook(name):
-        def f(mod, inp, out):
-            if name not in seen:
-                seen[name] = (inp[0].detach().clone(), out.detach().clone())
-        return f
-    names = ['llm.1.self_attn.k_proj', 'dit.2.adaln', 'dit.0.attn1.v_proj']
-    hs = [model.get_submodule(nm).register_forward_hook(hook(nm)) for nm in names]
     with torch.no_grad():
-        model(*obs)
-    for h in hs:
-        h.remove()
-    for nm in names:
-        L = layers[nm]
-        x, y = seen[nm]
-        ref = O.Layer(n(L.bits).view(np.uint16), n(L.tlut), n(L.row_scale), n(L.su), n(L.sv))
-        yr = O.reference_linear(n(x.reshape(-1, L.n)), 'bf16', ref)
-        assert np.array_equal(n(y.reshape(-1, L.m)), yr), nm
+        outs['unfused'] = model(*obs)
+    torch.cuda.synchronize()
+    for k, v in outs.items():
+        assert torch.equal(v, outs['fly']), k

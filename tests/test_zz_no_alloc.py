@@ -32,7 +32,9 @@ def lib():
     return _lib
 
 
-@pytest.mark.parametrize('M,N,K', [(1, 4096, 4096), (5, 1536, 1152), (16, 2048, 2048)])
+# (16, 32768, 256) fills the scratch array exactly: M * N partial sums plus N / 16 arrival counters end at its last
+# element.
+@pytest.mark.parametrize('M,N,K', [(1, 4096, 4096), (5, 1536, 1152), (16, 2048, 2048), (16, 32768, 256)])
 def test_noalloc_matches_workspace_entry(lib, M, N, K):
     dev = torch.device('cuda')
     tens, _ = cases.layer_tensors(f'noalloc{N}x{K}', N, K)
@@ -68,4 +70,5 @@ def test_noalloc_rejects_oversize(lib):
     assert limit == 16 * 32768
     a = ctypes.c_void_p(1 << 20)
     assert lib.lib.tcq_gemm_tcq_noalloc(a, a, a, a, a, a, 16, 65536, 64, 1 << 30, 1 << 30, None) == 1      # N too large
+    assert lib.lib.tcq_gemm_tcq_noalloc(a, a, a, a, a, a, 1, 32768 + 16, 64, 1 << 30, 1 << 30, None) == 1  # one tile row past the limit
     assert lib.lib.tcq_gemm_tcq_noalloc(a, a, a, a, a, a, 17, 1024, 64, 1 << 30, 1 << 30, None) == 1       # M > 16

@@ -629,11 +629,16 @@ constexpr int kMaxDevices = 64;
 int* g_scratch_addr[kMaxDevices];
 std::mutex g_scratch_mu;
 
-int scratch_for_current_device(int** out) {
+// The address is looked up again on every call whose stream is not capturing (a host-side lookup once the module is
+// loaded), so a device reset that reloads the module never leaves a stale address behind; during a capture the last
+// address looked up on this device is used.
+int scratch_for_current_device(int** out, cudaStream_t st) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TCQ_ERR_DEVICE;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return TCQ_ERR_DEVICE;
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!g_scratch_addr[dev] || cap == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_gemv_scratch) != cudaSuccess || !p) return TCQ_ERR_DEVICE;
         g_scratch_addr[dev] = reinterpret_cast<int*>(p);
@@ -712,11 +717,13 @@ size_t tcq_gemm_tcq_noalloc_max_elements(void) { return (size_t)kNoAllocMaxMN; }
 // without the workspace. Callers in this position are, for example, a robot's real-time control loop that must not
 // call cudaMalloc (it may synchronize the device and take an unbounded time in the middle of an action step), or a
 // host framework's plugin interface that owns every device buffer and hands the plugin only its inputs and outputs.
-// The stream-K scratch is the fixed array g_gemv_scratch; its device address is resolved on the first call on each
-// device (so that first call should come before any stream capture). Limits: 1 <= M <= 16, N <= 32768,
-// M * N <= 524288; larger shapes return TCQ_ERR_SHAPE. All calls share the one array per device: the used part is
-// cleared (cudaMemsetAsync, no allocation) on the caller's stream before the kernel, and calls that overlap on the GPU
-// (other streams, other host threads) race on it. Allocates nothing: no cudaMalloc / cudaFree / library allocation.
+// The stream-K scratch is the fixed array g_gemv_scratch; its device address is looked up on every call outside a
+// stream capture, and a call inside a capture uses the address of the last call on that device (so the first call on
+// a device should come before any stream capture). Limits: 1 <= M <= 16, N <= 32768, M * N <= 524288; larger shapes
+// return TCQ_ERR_SHAPE. All calls share the one array per device: the used part is cleared (cudaMemsetAsync, no
+// allocation) on the caller's stream before the kernel, and calls that overlap on the GPU (other streams, other host
+// threads) race on it. If the kernel launch itself then fails (TCQ_ERR_LAUNCH), that clear is already queued; it
+// touches only the library's own array. Allocates nothing: no cudaMalloc / cudaFree / library allocation.
 int tcq_gemm_tcq_noalloc(const uint16_t* bits, const int8_t* t8, const int32_t* q4, const float* s, const float* rs, float* z,
                          int M, int N, int K, int nb0, int nb1, void* stream) {
     if (!bits || !t8 || !q4 || !s || !rs || !z) return TCQ_ERR_ARG;
@@ -724,10 +731,10 @@ int tcq_gemm_tcq_noalloc(const uint16_t* bits, const int8_t* t8, const int32_t* 
     if (N > kNoAllocMaxN || (long long)M * N > kNoAllocMaxMN) return TCQ_ERR_SHAPE;
     if (!tcq_aligned(bits, 16) || !tcq_aligned(q4, 4) || !tcq_aligned(t8, 16)) return TCQ_ERR_ALIGN;
     if (nb0 < 0 || nb1 < 0) return TCQ_ERR_ARG;
-    int* ws = nullptr;
-    const int e = scratch_for_current_device(&ws);
-    if (e) return e;
     cudaStream_t st = (cudaStream_t)stream;
+    int* ws = nullptr;
+    const int e = scratch_for_current_device(&ws, st);
+    if (e) return e;
     if (cudaMemsetAsync(ws, 0, tcq_gemm_tcq_workspace(M, N), st) != cudaSuccess) return TCQ_ERR_LAUNCH;
     return dispatch_gemm_tcq(bits, t8, q4, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }

@@ -9,8 +9,10 @@ blocks), AdaLN conditioned on the flow timestep, 4 flow-matching Euler steps pro
 64-dim state. Attention, norms, embeddings and the small input / output projections are PyTorch BF16; the quantized
 Linears are `modules.KLinear` / `KGatedMLP` / `KPlainMLP` (2-bit trellis, W2A8) and `W8A8Linear` (vision).
 
-Oracle for the whole policy: the same model with runtime='reference' (every quantized Linear replaced by the W2A8 /
-W8A8 definition in PyTorch ops), as the reference does with its RefLinear runtime (modules.py:209-219).
+Oracle for the whole policy: the same model with runtime='reference', as the reference does with its RefLinear
+runtime (modules.py:209-219): every quantized Linear is the W2A8 / W8A8 definition in PyTorch ops (`definition`:
+PyTorch-ops trellis decode, cuBLASLt INT8 products through torch._int_mm), and the norms and the rotary embedding
+are PyTorch ops too. Nothing of the kernel library runs in it.
 """
 import math
 from dataclasses import dataclass
@@ -18,6 +20,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import definition
 from . import kernels as K
 from . import modules
 from .tcq_format import Layer
@@ -100,14 +103,8 @@ class W8A8Linear(torch.nn.Module):
             return y.reshape(*shape[:-1], -1)
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
-        if self.reference:                                     # the definition in PyTorch ops (tcq_format.py:119-122)
-            h = x2.float()
-            amax = h.abs().amax(dim=1, keepdim=True)
-            s = torch.where(amax > 0, amax / torch.full_like(amax, 127.0), torch.ones_like(amax))
-            q = torch.clamp(torch.round(h / s), -127, 127).to(torch.int8)
-            y = ((K.int_mm(q, self.W).float() * s) * self.s_ch[None, :]).to(torch.bfloat16)
-            if self.bias is not None:
-                y = y + self.bias
+        if self.reference:                                     # the definition in PyTorch ops (tcq_format.py:119-135)
+            y = definition.w8a8_linear(x2, self.W, self.s_ch, self.bias)
             if act == 'gelu':
                 y = F.gelu(y, approximate='tanh')
         else:
@@ -165,7 +162,9 @@ def _norm(norm, kind, x, delta, weight, bias, eps, mod=None, mod_rows=1):
     """Residual add + norm of a block boundary. delta: None, a BF16 tensor, or a modules.Deferred (the producing
     layer's post not yet run). With a consumer group wired to the norm (`norm.consumer`), the next layer's rotation +
     quantization runs in the same kernel and the normed activation is returned as a modules.QAct for that group.
-    Returns (x + delta, normed activation)."""
+    Returns (x + delta, normed activation). The reference runtime's norms (`torch_ops`) are PyTorch ops."""
+    if getattr(norm, 'torch_ops', False):
+        return definition.add_norm(x, delta, weight, bias, eps, kind, mod=mod, mod_rows=mod_rows)
     consumer = getattr(norm, 'consumer', None)
     if getattr(norm, 'w8_consumer', False) and not isinstance(delta, modules.Deferred) and mod is None:
         # W8A8 consumers: the norm quantizes its output per token in the same kernel (no rotation)
@@ -270,7 +269,10 @@ class LlmBlock(torch.nn.Module):
         a = self.self_attn
         q, k, v = a.q_proj(h), a.k_proj(h), a.v_proj(h)
         cos, sin = rope
-        q, k = K.rope(q, cos, sin, self.heads, out=q), K.rope(k, cos, sin, self.kv_heads, out=k)
+        if getattr(self, 'torch_ops', False):
+            q, k = definition.rope(q, cos, sin, self.heads), definition.rope(k, cos, sin, self.kv_heads)
+        else:
+            q, k = K.rope(q, cos, sin, self.heads, out=q), K.rope(k, cos, sin, self.kv_heads, out=k)
         o = _attention(q, k, v, self.heads, self.kv_heads, causal=True)
         x, h = self.post_attention_layernorm(x, a.o_proj(o))
         return x, self.mlp(h)
@@ -449,10 +451,11 @@ def synthetic_w8a8(model, device, seed=1, reference=False):
         modules.set_submodule(model, name, W8A8Linear(W, s_ch, bias, reference=reference))
 
 
-def build_policy(device='cuda', runtime='fly', c=PolicyConfig(), seed=0, layers=None):
+def build_policy(device='cuda', runtime='fly', c=PolicyConfig(), seed=0, layers=None, ref_w8=None):
     """The quantized policy on `device`. runtime: 'fly' (2-bit stream decoded inside the products), 'resident' (INT8
     decoded once), 'hybrid' (DiT decoded once per chunk via modules.decode_chunk) or 'reference' (the definition in
-    PyTorch ops). Returns (policy, trellis layers, install info)."""
+    PyTorch ops, with norms and rotary embedding in PyTorch ops; ref_w8 optionally gives its decoded weights).
+    Returns (policy, trellis layers, install info)."""
     model = GrootStylePolicy(c)
     _fp_init(model, seed)
     model = model.to(device=device, dtype=torch.bfloat16)
@@ -463,8 +466,12 @@ def build_policy(device='cuda', runtime='fly', c=PolicyConfig(), seed=0, layers=
         mlp_acts[f'llm.{i}.mlp'] = 'silu'
     for i in range(c.dit_layers):
         mlp_acts[f'dit.{i}.ff'] = 'gelu'
-    info = modules.install(model, layers, runtime=runtime, chunk_parts=('dit.',), mlp_acts=mlp_acts)
+    info = modules.install(model, layers, runtime=runtime, chunk_parts=('dit.',), mlp_acts=mlp_acts, ref_w8=ref_w8)
     info['chains'] = wire_chains(model) if runtime != 'reference' and modules.FUSE['chain'] else 0
+    if runtime == 'reference':
+        for m in model.modules():
+            if isinstance(m, (RMSNorm, LayerNorm, LlmBlock)):
+                m.torch_ops = True
     model.eval()
     return model, layers, info
 
@@ -477,15 +484,15 @@ def wire_chains(model):
 
     def consume(norm, target):
         nonlocal wired
-        group = target.group[0] if isinstance(target, modules.KLinear) else \
+        group = target.shared if isinstance(target, modules.KLinear) else \
             target.groups[0] if isinstance(target, (modules.KGatedMLP, modules.KPlainMLP)) else None
         if group is not None:
             norm.consumer = group
             wired += 1
 
     def defer(producer):
-        if isinstance(producer, modules.KLinear) and len(producer.group[0].layers) == 1:
-            producer.group[0].defer = True
+        if isinstance(producer, modules.KLinear) and len(producer.shared.layers) == 1:
+            producer.shared.defer = True
         elif isinstance(producer, (modules.KGatedMLP, modules.KPlainMLP)):
             producer.defer = True
 

@@ -1,72 +1,90 @@
-"""Kernel-class breakdown of one CUDA-graph replay (the reference's runner.kernel_classes, runner.py:227-266).
+"""Where one CUDA-graph replay spends its time, by kernel class, and small seeded kernel cases for a profiler.
 
-A torch.profiler (CUPTI) trace of a single replay; device time per kernel class, launch counts, wall time and the
-gaps between kernels, plus each class's share of the critical path (a kernel's time from the previous kernel's end to
-its own end: with programmatic dependent launch a kernel's own time range includes its wait for the predecessor).
-Classes are matched by regex on the kernel name, first match wins.
+`replay_breakdown(graph)` traces a single replay with torch.profiler (CUPTI) and attributes every device kernel to a
+class (`classify`). Besides each class's device time it reports each class's share of the critical path: walking the
+kernels in start order, a kernel is charged only for the time by which it moves the end of the work done so far
+(with programmatic dependent launch a kernel starts early and waits for its predecessor inside its own time range,
+so its raw duration overstates what it costs). What the replay spends outside every kernel is the idle time.
 """
 import re
-from collections import Counter, defaultdict
+from collections import defaultdict
 
 import torch
 
-CLASSES = [
-    ('trellis decode-GEMV (SIMT)', r'k_gemm_tcq<'),
-    ('trellis decode-GEMM (tcgen05)', r'k_gemm_tcq_tc'),
-    ('trellis decode', r'k_decode'),
-    ('INT8 GEMM (tcgen05)', r'k_gemm_i8'),
-    ('INT8-resident GEMV', r'k_gemm_w8'),
-    ('rotate + quantize', r'k_pre|k_quant'),
-    ('post + add + norm + pre chain', r'k_chain'),
-    ('scale + rotate', r'k_post'),
-    ('MLP middles', r'k_mid'),
-    ('attention', r'flash|fmha|attention|softmax|sdpa'),
-    ('matrix product (BF16, cuBLAS)', r'gemm|cutlass|cublas|Gemv|gemv|matmul|nvjet'),
-    ('norm', r'rms|layer_norm|LayerNorm|norm'),
-    ('copies / casts', r'copy|cast|Copy|fill|zero|memset|Memset|memcpy|Memcpy'),
-    ('NCCL', r'nccl'),
-    ('other elementwise', r'.*'),
-]
+# (class, name fragments) in priority order: a kernel belongs to the first class one of whose fragments its
+# (demangled) name contains; names matching nothing are 'other'.
+_FRAGMENTS = (
+    ('trellis decode-GEMV (SIMT)', ('k_gemm_tcq<',)),
+    ('trellis decode-GEMM (tcgen05)', ('k_gemm_tcq_tc',)),
+    ('trellis decode', ('k_decode',)),
+    ('INT8 GEMM (tcgen05)', ('k_gemm_i8',)),
+    ('INT8-resident GEMV', ('k_gemm_w8',)),
+    ('rotate + quantize', ('k_pre', 'k_quant')),
+    ('post + add + norm + pre chain', ('k_chain',)),
+    ('scale + rotate', ('k_post',)),
+    ('MLP middles', ('k_mid',)),
+    ('residual add + norm', ('k_addnorm', 'k_add_norm')),
+    ('rotary embedding', ('k_rope',)),
+    ('attention', ('flash', 'fmha', 'attention', 'softmax', 'sdpa', 'cudnn')),
+    ('BF16 matrix product (cuBLAS)', ('gemm', 'Gemm', 'gemv', 'Gemv', 'cublas', 'nvjet', 'cutlass', 'matmul')),
+    ('NCCL', ('nccl', 'Nccl')),
+    ('memory copies and fills', ('memcpy', 'Memcpy', 'memset', 'Memset', 'copy_', 'fill_', 'zero_')),
+)
 
 
-def kernel_classes(graph, warm=3):
-    """Profile one replay of `graph` (a torch.cuda.CUDAGraph). Returns a dict of times in ms."""
+def classify(kernel_name):
+    for cls, frags in _FRAGMENTS:
+        if any(f in kernel_name for f in frags):
+            return cls
+    return 'other'
+
+
+def _short(name, width=90):
+    return re.sub(r'\(anonymous namespace\)::', '', name)[:width]
+
+
+def replay_breakdown(graph, warm=3):
+    """Trace one replay of `graph` (a torch.cuda.CUDAGraph) after `warm` untraced ones. Returns times in ms: the
+    replay's wall time (CUDA events), total kernel time, idle time, launches, and per class the device time, the
+    critical-path share and the launch count, plus the heaviest kernels by each measure."""
     from torch.profiler import ProfilerActivity, profile
     for _ in range(warm):
         graph.replay()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
-        start.record()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as trace:
+        ev0.record()
         graph.replay()
-        end.record()
-        end.synchronize()
-    wall = start.elapsed_time(end)
-    by, launches, top = defaultdict(float), Counter(), Counter()
-    excl, excl_top = defaultdict(float), Counter()
-    kernels = sorted((e for e in prof.events() if e.device_type.name == 'CUDA'), key=lambda e: e.time_range.start)
-    prev_end = None
-    for e in kernels:
-        dur = e.time_range.elapsed_us() / 1000
-        cls = next(c for c, pat in CLASSES if re.search(pat, e.name))
-        by[cls] += dur
-        launches[cls] += 1
-        name = e.name.replace('(anonymous namespace)::', '')[:90]
-        top[name] += dur
-        # Kernels launched early by programmatic dependent launch wait for their predecessor inside their own time
-        # range, so a kernel's share of the critical path is the time from the previous kernel's end to its own end.
-        t0, t1 = e.time_range.start, e.time_range.end
-        x = (t1 - max(t0, prev_end if prev_end is not None else t0)) / 1000
-        if x > 0:
-            excl[cls] += x
-            excl_top[name] += x
-        prev_end = t1 if prev_end is None else max(prev_end, t1)
-    total = sum(by.values())
-    return dict(wall_ms=wall, kernel_ms=total, gaps_ms=max(wall - sum(excl.values()), 0.0), launches=sum(launches.values()),
-                by_class_ms={k: round(v, 3) for k, v in sorted(by.items(), key=lambda kv: -kv[1])},
-                critical_path_ms_by_class={k: round(v, 3) for k, v in sorted(excl.items(), key=lambda kv: -kv[1])},
-                launches_by_class=dict(launches), top=[(nm, round(d, 3)) for nm, d in top.most_common(12)],
-                critical_path_top=[(nm, round(d, 3)) for nm, d in excl_top.most_common(16)])
+        ev1.record()
+        ev1.synchronize()
+    replay_ms = ev0.elapsed_time(ev1)
+    spans = sorted(((e.time_range.start, e.time_range.end, e.name) for e in trace.events() if e.device_type.name == 'CUDA'),
+                   key=lambda sp: sp[0])
+    device = defaultdict(float)
+    critical = defaultdict(float)
+    count = defaultdict(int)
+    by_kernel = defaultdict(float)
+    by_kernel_critical = defaultdict(float)
+    frontier = None                         # latest end among the kernels seen so far (microseconds)
+    for t0, t1, name in spans:
+        cls, key = classify(name), _short(name)
+        dur = (t1 - t0) / 1000.0
+        device[cls] += dur
+        count[cls] += 1
+        by_kernel[key] += dur
+        gain = (t1 - max(t0, frontier)) / 1000.0 if frontier is not None else dur
+        if gain > 0:
+            critical[cls] += gain
+            by_kernel_critical[key] += gain
+        frontier = t1 if frontier is None else max(frontier, t1)
+
+    def ranked(d, n=None):
+        items = sorted(d.items(), key=lambda kv: kv[1], reverse=True)[:n]
+        return {k: round(v, 3) for k, v in items}
+    busy = sum(critical.values())
+    return dict(replay_ms=replay_ms, kernel_ms=sum(device.values()), idle_ms=max(replay_ms - busy, 0.0), launches=len(spans),
+                device_ms_by_class=ranked(device), critical_ms_by_class=ranked(critical), launches_by_class=dict(count),
+                heaviest=list(ranked(by_kernel, 12).items()), heaviest_critical=list(ranked(by_kernel_critical, 16).items()))
 
 
 # ----------------------------------------------------------------------------------------------- profiling cases
@@ -76,7 +94,7 @@ def kernel_classes(graph, warm=3):
 #   python -m yanlongvla_b200.profile pre|rotate [--m 4096] [--k 4096] [--launches 4]
 #   python -m yanlongvla_b200.profile chain [--m 17] [--k 1536] [--launches 6]
 #   python -m yanlongvla_b200.profile gemv_tc [--n 1536] [--k 1536] [--tokens 17] [--launches 4]
-#   python -m yanlongvla_b200.profile policy [--tokens 1]    (kernel_classes of one chunk-graph replay, as JSON)
+#   python -m yanlongvla_b200.profile policy [--tokens 1]    (replay_breakdown of one chunk-graph replay, as JSON)
 # `gemv` runs kernels.gemm_tcq on one trellis layer (uniform random streams, a snapped table), `gemm` runs
 # kernels.int_mm (INT32 out) or kernels.int8_gemm (BF16 out with the scale epilogue) on uniform INT8 operands. Every launch of a case is identical, so the ones after the first two
 # are warm in the driver and the code caches.
@@ -166,7 +184,7 @@ def _case_chain(m, n, launches):
 
 
 def _case_policy(batch):
-    """kernel_classes of one CUDA-graph replay of the fly policy's action chunk for `batch` observations."""
+    """replay_breakdown of one CUDA-graph replay of the fly policy's action chunk for `batch` observations."""
     import json
     from . import policy as P
     c = P.PolicyConfig()
@@ -181,7 +199,7 @@ def _case_policy(batch):
     g = torch.cuda.CUDAGraph()
     with torch.no_grad(), torch.cuda.graph(g):
         model(*obs)
-    print(json.dumps(kernel_classes(g), indent=1))
+    print(json.dumps(replay_breakdown(g), indent=1))
 
 
 def main(argv=None):
