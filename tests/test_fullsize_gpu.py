@@ -94,7 +94,8 @@ def test_config2_full_rotation(K, D):
 def test_config4_full_policy_every_layer_and_chunk(K):
     """Config 4 at full depth, B = 1: all 442 quantized layers (280 W2A8, 162 W8A8) reproduce the definition's
     intermediates bit for bit on the inputs they receive in the reference-runtime policy; three of the decodes are
-    also checked against the CPU oracle; the fly chunk is within the task's tolerance of the reference chunk."""
+    also checked against the CPU oracle; the fly chunk is within the task's tolerance of the reference chunk, and equal
+    to it bit for bit."""
     import policy_parity as PP
     from yanlongvla_b200 import policy as P
     c = P.PolicyConfig()
@@ -118,3 +119,4 @@ def test_config4_full_policy_every_layer_and_chunk(K):
     torch.cuda.synchronize()
     ok, max_rel, cos = PP.within_tolerance(a, a_ref)
     assert torch.isfinite(a).all() and ok, f'max-abs / RMS {max_rel.tolist()}, cosine {cos.tolist()}'
+    assert torch.equal(a, a_ref), f'within tolerance but not bit-exact: max-abs / RMS {max_rel.tolist()}'

@@ -5,8 +5,8 @@ nothing of the kernel library.
   * every quantized layer, on the input it receives inside the reference policy, reproduces the definition's
     intermediates bit for bit through the kernels (tests/policy_parity.py; the reference's parity.py:22-73);
   * whole action chunks of every kernel runtime are within the task's tolerance of the reference chunk, per
-    observation (max-abs <= 1e-2 x RMS, cosine >= 0.9995), at B = 1 and B = 8: the norms' row sums run in a
-    different order in the kernels, so chunks agree to that tolerance rather than bit for bit;
+    observation (max-abs <= 1e-2 x RMS, cosine >= 0.9995), at B = 1 and B = 8, and in fact bit for bit: the
+    reference runtime's norms sum their rows in the kernels' fixed order (`definition.row_sum`);
   * the kernel runtimes agree with one another bit for bit, and the fused block-boundary chains equal the separate
     post / add-norm / pre kernels bit for bit.
 """
@@ -59,6 +59,7 @@ def test_chunk_within_tolerance(small, runtime, B):
     assert torch.isfinite(a).all()
     ok, max_rel, cos = PP.within_tolerance(a, a_ref)
     assert ok, f'max-abs / RMS {max_rel.tolist()}, cosine {cos.tolist()}'
+    assert torch.equal(a, a_ref), f'within tolerance but not bit-exact: max-abs / RMS {max_rel.tolist()}'
 
 
 def test_kernel_runtimes_agree_and_chains_equal_unfused(small):

@@ -16,8 +16,8 @@ sm_100a library, so a comparison against it checks the kernels against an indepe
   linear           the whole layer, y = BF16(walsh(((acc * s) * rs)) * sv + bias)                  (tcq_format.py:125-148)
 
 and, for the policy's own glue between quantized layers, the residual add + RMSNorm / LayerNorm (+ AdaLN) and the
-half-split rotary embedding in PyTorch ops. The kernels compute the norms' row sums in their own fixed order, so
-those agree with these to about one BF16 rounding; everything else here is bit-exact against the kernels.
+half-split rotary embedding in PyTorch ops. A norm's row sums are taken in one fixed order (`row_sum`), the one the
+norm kernels use, so that the whole policy can be compared bit for bit.
 """
 import math
 
@@ -128,26 +128,58 @@ def w8a8_linear(x, W, s_ch, bias=None):
     return y.reshape(*shape[:-1], W.shape[0])
 
 
+def _norm_threads(D):
+    """Threads of one row in the kernels' canonical order: one 16-element chunk each, a multiple of 32, 32..512."""
+    return min(max(-(-(D // 16) // 32) * 32, 32), 512)
+
+
+def row_sum(v):
+    """Sum of each row of v (M, D) FP32 in one fixed order (the order the norm kernels use, so that a norm computed
+    here and one computed there agree bit for bit): the row is cut into 16-element chunks; chunk c belongs to thread
+    c mod T (T = _norm_threads(D); D > 8192 wraps four chunks onto each thread), and each thread keeps one running sum
+    over its chunks' elements in index order, starting from 0; the threads' sums are combined within each group of 32
+    by halving (element i of the first half plus element i of the second half, five times); the 32-groups' results
+    are added in group order, starting from 0."""
+    M, D = v.shape
+    T = _norm_threads(D)
+    NC = 1 if D <= 8192 else 4
+    chunks = torch.zeros(M, NC * T, 16, dtype=torch.float32, device=v.device)
+    chunks[:, :D // 16] = v.reshape(M, D // 16, 16)
+    per_thread = chunks.view(M, NC, T, 16).transpose(1, 2).reshape(M, T, NC * 16)
+    part = torch.zeros(M, T, dtype=torch.float32, device=v.device)
+    for i in range(NC * 16):
+        part = part + per_thread[:, :, i]
+    g = part.view(M, T // 32, 32)
+    while g.shape[-1] > 1:
+        half = g.shape[-1] // 2
+        g = g[..., :half] + g[..., half:]
+    total = torch.zeros(M, dtype=torch.float32, device=v.device)
+    for w in range(T // 32):
+        total = total + g[:, w, 0]
+    return total[:, None]
+
+
 def add_norm(x, delta, weight, bias, eps, kind, mod=None, mod_rows=1):
     """Residual add + norm in PyTorch ops: h = BF16(x + delta) (x when delta is None), n = BF16(norm(h)) with
-    RMSNorm n = (h * rsqrt(mean(h^2) + eps)) * w or LayerNorm n = ((h - mean) * rsqrt(var + eps)) * w + b (FP32,
-    biased variance), then the AdaLN modulation n * (1 + scale) + shift when mod = (scale, shift) (one (D,) row per
-    mod_rows rows). Returns (h, n)."""
+    RMSNorm n = (h * r) * w, r = rsqrt(sum(h^2) / D + eps), or LayerNorm n = ((h - mu) * r) * w + b, mu = sum(h) / D,
+    r = rsqrt(sum((h - mu)^2) / D + eps) (FP32; true divisions; the sums in `row_sum`'s fixed order), then the AdaLN
+    modulation n * (1 + scale) + shift when mod = (scale, shift) (one (D,) row per mod_rows rows). Returns (h, n)."""
     h = x if delta is None else x + delta
     D = h.shape[-1]
     hf = h.reshape(-1, D).float()
+    div = torch.full((hf.shape[0], 1), float(D), dtype=torch.float32, device=hf.device)
     if kind == 'rms':
-        n = hf * torch.rsqrt(hf.pow(2).mean(dim=1, keepdim=True) + eps)
-        if weight is not None:
-            n = n * weight.float()
+        r = torch.rsqrt(row_sum(hf * hf) / div + eps)
+        n = hf * r
     else:
-        mu = hf.mean(dim=1, keepdim=True)
+        mu = row_sum(hf) / div
         c = hf - mu
-        n = c * torch.rsqrt(c.pow(2).mean(dim=1, keepdim=True) + eps)
-        if weight is not None:
-            n = n * weight.float()
-        if bias is not None:
-            n = n + bias.float()
+        r = torch.rsqrt(row_sum(c * c) / div + eps)
+        n = c * r
+    if weight is not None:
+        n = n * weight.float()
+    if bias is not None:
+        n = n + bias.float()
     if mod is not None:
         scale, shift = mod
         scale = scale.reshape(-1, D).float().repeat_interleave(mod_rows, dim=0)
