@@ -533,12 +533,14 @@ k_gemm_i8_2sm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
 // the decoded weights never leave the SM. One CTA = one 128-channel tile (8 tile rows) x one K range; per 128-byte K
 // stage, 16 decoder warps write the 128 x 128 INT8 A tile in the 128B-swizzled K-major UMMA layout (512 threads x 2
 // tile rows), TMA brings the BN x 128 activation tile, one thread issues four tcgen05.mma.kind::i8 (M = 128, N = BN,
-// K = 32) into TMEM. Epilogue (decoder warps 2..5, one TMEM lane quarter each): scale and store z, or, when K is split
-// over (at most kTcKsMax) CTAs, store INT32 partials into the split's own slice of the workspace (plain stores: no
-// atomics competing in L2); the CTA whose arrival completes a channel tile sums the slices with all its decoder
-// warps, writes z and zeroes the slices again.
+// K = 32) into TMEM. Epilogue: the 16 decoder warps copy the accumulator from TMEM into shared memory (the decode
+// table's space, dead by then); without a K split the CTA scales and writes z from there; the K splits of a channel
+// tile run as one thread-block cluster, and every rank sums one slice of the tile over all ranks' shared memory and
+// writes it. Only when no cluster fits do the splits store INT32 partials into their own workspace slices (plain
+// stores), and the CTA whose arrival completes a channel tile sums them, writes z and zeroes the slices again.
 constexpr int kTcDecWarps = 16;
 constexpr int kTcKsMax = 4;         // K splits per channel tile, at most (the finishing CTA sums that many slices)
+constexpr int kTcPrefetch = 4;      // K stages of weight words a decoder thread has in flight
 constexpr int kTcThreads = 64 + 32 * kTcDecWarps;
 
 struct TcParts {
@@ -598,8 +600,9 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
     }
     pdl_launch_dependents();
     // Decoder thread d -> tile (i, j) = (d >> 6, (d >> 3) & 7) of a K stage, tile rows 2g, 2g + 1 (g = d & 7). Its
-    // words of the first stage are requested before the table build (their DRAM latency hides under it), the next
-    // stage's while the current one is decoded.
+    // words of the first kTcPrefetch stages are requested before the table build (their DRAM latency hides under
+    // it); while stage kb is decoded, stage kb + kTcPrefetch is requested (a stage decodes in a fraction of the load
+    // latency, so one stage of look-ahead left the decoders waiting on every stage).
     const int dd = threadIdx.x - 64;
     const int di = dd >> 6, dj = (dd >> 3) & 7, dg = dd & 7;
     const bool drow_ok = warp >= 2 && tr0 + di < tiles_n;
@@ -613,8 +616,9 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             c = __ldg(tw + ((2 * dg + 2) & 15));
         }
     };
-    u32 nw0, nw1, nw2;
-    load_words(kb0, nw0, nw1, nw2);
+    u32 pw[kTcPrefetch][3];
+#pragma unroll
+    for (int p = 0; p < kTcPrefetch; ++p) load_words(kb0 + p, pw[p][0], pw[p][1], pw[p][2]);
     if (threadIdx.x < 8 && tr0 + (int)threadIdx.x < tiles_n && kb1 - kb0 > 1) {   // later stages: into L2 now
         const int t0 = (kb0 + 1) * 8, t1 = kb1 * 8 < tiles_k ? kb1 * 8 : tiles_k;
         if (t1 > t0)
@@ -665,9 +669,15 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         u32 ph = 0;
         for (int kb = kb0; kb < kb1; ++kb) {
             const int tc = kb * 8 + j;
-            const u32 w0 = nw0, w1 = nw1, w2 = nw2;
+            const u32 w0 = pw[0][0], w1 = pw[0][1], w2 = pw[0][2];
             const bool ok = drow_ok && tc < tiles_k;
-            load_words(kb + 1, nw0, nw1, nw2);
+#pragma unroll
+            for (int p = 0; p + 1 < kTcPrefetch; ++p) {
+                pw[p][0] = pw[p + 1][0];
+                pw[p][1] = pw[p + 1][1];
+                pw[p][2] = pw[p + 1][2];
+            }
+            load_words(kb + kTcPrefetch, pw[kTcPrefetch - 1][0], pw[kTcPrefetch - 1][1], pw[kTcPrefetch - 1][2]);
             if (!mbar_wait(empty0 + 8 * st, ph ^ 1, abort_flag)) break;
             uint8_t* a = sA + st * A_BYTES;
 #pragma unroll
@@ -681,67 +691,84 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             mbar_arrive(full0 + 8 * st);
             if (++st == STAGES) { st = 0; ph ^= 1; }
         }
-        // ---- epilogue: decoder warps 2..5 (warp index 4..7), one TMEM lane quarter each
-        if (warp >= 4 && warp < 8) {
+        // ---- epilogue
+        if (P.ks == 1 || P.cl) {
+            // Every decoder warp moves part of the accumulator from TMEM (its lane quarter warp & 3, column groups
+            // (warp - 2) / 4, + 4, ...) into shared memory, token-major [token][128 channels], in the space of the
+            // decode table: once the last MMA has completed, every decoder has arrived on its last stage, so no
+            // table lookup is left. Stores are unconditional (rows past M are never read).
+            if (mbar_wait(tfull, 0, abort_flag) && !*abort_flag) {
+                tc_fence_after();
+                const int q = warp & 3;
+                int* sp = reinterpret_cast<int*>(smem) + 32 * q + lane;
+                const int chunks = (M + 31) >> 5;
+#pragma unroll 1
+                for (int c = (warp - 2) >> 2; c < chunks; c += 4) {
+                    u32 v[32];
+                    tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(32 * c), v);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) sp[(32 * c + jj) * BM] = (int)v[jj];
+                }
+            }
+        } else if (warp >= 4 && warp < 8) {
+            // K split without a cluster: decoder warps 2..5 (warp index 4..7), one TMEM lane quarter each, store the
+            // INT32 partials into this split's own slice of the workspace (plain stores, no atomics)
             const int q = warp & 3;
             const int ch = ct * BM + 32 * q + lane;
             const bool chok = ch < N;
             if (mbar_wait(tfull, 0, abort_flag)) {
                 tc_fence_after();
-                const float r = chok ? rs[ch] : 0.f;
-                int* part = ws_acc + (size_t)ksi * M * N;    // this split's slice of the partial sums
+                int* part = ws_acc + (size_t)ksi * M * N;
 #pragma unroll 1
-                for (int c = 0; c < (BN + 31) / 32; ++c) {
+                for (int c = 0; c < (M + 31) / 32; ++c) {
                     u32 v[32];
                     tmem_ld32(tmem + ((u32)(32 * q) << 16) + (u32)(32 * c), v);
                     if (chok) {
 #pragma unroll
                         for (int jj = 0; jj < 32; ++jj) {
                             const int tok = 32 * c + jj;
-                            if (tok < M) {
-                                const size_t o = (size_t)tok * N + ch;
-                                if (P.ks == 1) z[o] = ((float)(int)v[jj] * s_tok[tok]) * r;
-                                else if (P.cl) reinterpret_cast<int*>(sA)[tok * BM + 32 * q + lane] = (int)v[jj];
-                                else part[o] = (int)v[jj];
-                            }
+                            if (tok < M) part[(size_t)tok * N + ch] = (int)v[jj];
                         }
                     }
                 }
             }
         }
     }
-    if (P.cl) {
-        // The K splits of a channel tile are one cluster and each left its partial sums in its own shared memory (the
-        // A stages, free once every MMA is done). The leader (rank 0) sums every rank's partials in rank order through
-        // distributed shared memory, 4 elements x ks ranks of loads in flight per thread; the second cluster barrier
-        // keeps the peers' shared memory alive until the leader has read it. Every thread reaches both barriers.
-        cluster_sync();
-        if (cluster_rank() == 0 && !*abort_flag && warp >= 2) {
-            const int t = threadIdx.x - 64;
-            const u32 base = smem_u32(sA);
-            for (int e0 = t; e0 < M * BM; e0 += 4 * 32 * kTcDecWarps) {
-                int vals[4][8];
+    if (P.ks == 1 || P.cl) {
+        // Scale and write z. Without a K split, from this CTA's shared memory. With one, the K splits of the channel
+        // tile are a cluster and each rank finishes one slice of the tile's (token, channel) elements, summing the
+        // ranks' partials through distributed shared memory (integers: exact in any order); the second cluster
+        // barrier keeps every rank's shared memory alive until all have read it. Every thread reaches the barriers.
+        if (P.cl) cluster_sync(); else __syncthreads();
+        if (!*abort_flag && warp >= 2) {
+            const int R = P.cl ? P.ks : 1, rank = P.cl ? (int)cluster_rank() : 0;
+            const int E = M * BM, e_end = (int)((long long)E * (rank + 1) / R);
+            const u32 base = smem_u32(smem);
+            constexpr int NT = 32 * kTcDecWarps, U = 4;
+            for (int e0 = (int)((long long)E * rank / R) + (int)threadIdx.x - 64; e0 < e_end; e0 += U * NT) {
+                int vals[U][8];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int e = e0 + u * 32 * kTcDecWarps;
-                    const bool ok = e < M * BM && ct * BM + e % BM < N;
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * NT;
 #pragma unroll
-                    for (int r = 0; r < 8; ++r) vals[u][r] = ok && r < P.ks ? ld_cluster_s32(map_to_rank(base + 4u * e, r)) : 0;
+                    for (int r = 0; r < 8; ++r)
+                        vals[u][r] = e < e_end && r < R ? (P.cl ? ld_cluster_s32(map_to_rank(base + 4u * e, r))
+                                                                : reinterpret_cast<const int*>(smem)[e])
+                                                        : 0;
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int e = e0 + u * 32 * kTcDecWarps, tok = e / BM, ch = ct * BM + e % BM;
-                    if (e < M * BM && ch < N) {
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * NT, tok = e / BM, ch = ct * BM + e % BM;
+                    if (e < e_end && ch < N) {
                         int sum = 0;
 #pragma unroll
-                        for (int r = 0; r < 8; ++r)
-                            if (r < P.ks) sum += vals[u][r];
+                        for (int r = 0; r < 8; ++r) sum += vals[u][r];
                         z[(size_t)tok * N + ch] = ((float)sum * s_tok[tok]) * rs[ch];
                     }
                 }
             }
         }
-        cluster_sync();
+        if (P.cl) cluster_sync();
     }
     // Split K without a cluster: every CTA has stored its partials; the one whose arrival completes the channel tile
     // finishes it. The decision sits between two CTA-wide barriers that every thread reaches on every path.
@@ -960,14 +987,15 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     TcParts P;
     P.ct = (N + BM - 1) / BM;
     P.kb = (K + BK - 1) / BK;
-    // K splits. Token tiles of 32: the splits of a channel tile form a cluster (at most 8, a portable size) that
-    // reduces in distributed shared memory: the largest split with at least 3 K stages per CTA whose clusters are all
-    // resident at once (one CTA fills an SM, so clusters pack into the GPCs only so far). Otherwise, and for wider
-    // token tiles, the splits reduce through workspace slices (at most kTcKsMax).
+    // K splits: the splits of a channel tile form a cluster (at most 8, a portable size) that reduces in distributed
+    // shared memory, each rank finishing one slice of the tile: the largest split with at least 3 K stages per CTA
+    // (2 for token tiles wider than 32) whose clusters are all resident at once (one CTA fills an SM, so clusters pack
+    // into the GPCs only so far). When no cluster of 2 or more fits, the splits reduce through workspace slices (at
+    // most kTcKsMax).
     int ks = 1;
     bool cl = false;
-    if (BN == 32) {
-        int c = std::min({8, sms() / P.ct, P.kb, (P.kb + 2) / 3});
+    {
+        int c = std::min({8, sms() / P.ct, P.kb, BN == 32 ? (P.kb + 2) / 3 : P.kb / 2});
         for (; c >= 2; --c)
             if (P.ct <= max_clusters(kern, smem, c)) break;
         if (c >= 2) {
