@@ -548,8 +548,16 @@ struct TcParts {
     int ks;         // K splits per channel tile
     int kb;         // 128-byte K stages
     int nb0, nb1;   // layer bounds in tile rows (multiples of 8)
-    int cl;         // the K splits of a channel tile are one thread-block cluster (ks > 1, token tiles of 32)
+    int cl;         // the K splits of a channel tile are one thread-block cluster
+    int zvec;       // z is 16-byte aligned: the finished outputs leave as 16-byte stores
 };
+
+// 16 bytes of a cluster peer's (or this CTA's) shared memory.
+__device__ __forceinline__ int4 ld_cluster_v4(u32 addr) {
+    int4 v;
+    asm volatile("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ int ld_cluster_s32(u32 addr) {
     int v;
@@ -584,7 +592,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
 
     if (threadIdx.x == 0) {
         for (int st = 0; st < STAGES; ++st) {
-            mbar_init(full0 + 8 * st, 32 * kTcDecWarps + 1);
+            mbar_init(full0 + 8 * st, kTcDecWarps + 1);        // one arrival per decoder warp + the TMA
             mbar_init(empty0 + 8 * st, 1);
         }
         mbar_init(tfull, 1);
@@ -688,7 +696,8 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
                 *reinterpret_cast<uint4*>(a + row * 128 + ((j ^ (row & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor-core reads
-            mbar_arrive(full0 + 8 * st);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full0 + 8 * st);
             if (++st == STAGES) { st = 0; ph ^= 1; }
         }
         // ---- epilogue
@@ -739,31 +748,53 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         // tile are a cluster and each rank finishes one slice of the tile's (token, channel) elements, summing the
         // ranks' partials through distributed shared memory (integers: exact in any order); the second cluster
         // barrier keeps every rank's shared memory alive until all have read it. Every thread reaches the barriers.
+        // The tile's row scales and the token scales go to shared memory (the A stages, free once the last MMA has
+        // completed) before the barrier, so the reduction below reads every operand on chip.
+        float* s_rs = reinterpret_cast<float*>(sA);
+        float* s_st = s_rs + BM;
+        if (!*abort_flag && warp >= 2) {
+            for (int i = threadIdx.x - 64; i < BM + M; i += 32 * kTcDecWarps) {
+                if (i < BM) s_rs[i] = ct * BM + i < N ? rs[ct * BM + i] : 0.f;
+                else s_st[i - BM] = s_tok[i - BM];
+            }
+        }
         if (P.cl) cluster_sync(); else __syncthreads();
         if (!*abort_flag && warp >= 2) {
             const int R = P.cl ? P.ks : 1, rank = P.cl ? (int)cluster_rank() : 0;
-            const int E = M * BM, e_end = (int)((long long)E * (rank + 1) / R);
-            const u32 base = smem_u32(smem);
-            constexpr int NT = 32 * kTcDecWarps, U = 4;
-            for (int e0 = (int)((long long)E * rank / R) + (int)threadIdx.x - 64; e0 < e_end; e0 += U * NT) {
-                int vals[U][8];
+            // groups of 4 consecutive channels of one token: one 16-byte load per rank and group, U groups in flight
+            const int G = M * (BM / 4), g_end = (int)((long long)G * (rank + 1) / R);
+            u32 peer[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) peer[r] = r < R ? (P.cl ? map_to_rank(smem_u32(smem), r) : smem_u32(smem)) : 0u;
+            constexpr int NT = 32 * kTcDecWarps, U = 8;
+            for (int g0 = (int)((long long)G * rank / R) + (int)threadIdx.x - 64; g0 < g_end; g0 += U * NT) {
+                int4 sum[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * NT;
+                    const int g = g0 + u * NT;
+                    sum[u] = make_int4(0, 0, 0, 0);
+                    if (g < g_end) {
 #pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        vals[u][r] = e < e_end && r < R ? (P.cl ? ld_cluster_s32(map_to_rank(base + 4u * e, r))
-                                                                : reinterpret_cast<const int*>(smem)[e])
-                                                        : 0;
+                        for (int r = 0; r < 8; ++r)
+                            if (r < R) {
+                                const int4 a = ld_cluster_v4(peer[r] + 16u * g);
+                                sum[u].x += a.x; sum[u].y += a.y; sum[u].z += a.z; sum[u].w += a.w;
+                            }
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * NT, tok = e / BM, ch = ct * BM + e % BM;
-                    if (e < e_end && ch < N) {
-                        int sum = 0;
-#pragma unroll
-                        for (int r = 0; r < 8; ++r) sum += vals[u][r];
-                        z[(size_t)tok * N + ch] = ((float)sum * s_tok[tok]) * rs[ch];
+                    const int g = g0 + u * NT, tok = g >> 5, c = 4 * (g & 31);
+                    if (g < g_end && ct * BM + c < N) {
+                        const float st = s_st[tok];
+                        const float4 o = make_float4(((float)sum[u].x * st) * s_rs[c], ((float)sum[u].y * st) * s_rs[c + 1],
+                                                     ((float)sum[u].z * st) * s_rs[c + 2], ((float)sum[u].w * st) * s_rs[c + 3]);
+                        float* zo = z + (size_t)tok * N + ct * BM + c;
+                        if (P.zvec) {
+                            *reinterpret_cast<float4*>(zo) = o;
+                        } else {
+                            zo[0] = o.x; zo[1] = o.y; zo[2] = o.z; zo[3] = o.w;
+                        }
                     }
                 }
             }
@@ -1006,6 +1037,7 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     if (!cl) ks = std::max(1, std::min({kTcKsMax, sms() / P.ct, P.kb}));
     P.ks = ks;
     P.cl = cl ? 1 : 0;
+    P.zvec = tcq_aligned(z, 16) ? 1 : 0;
     P.nb0 = nb0;
     P.nb1 = nb1;
     cudaLaunchConfig_t cfg = {};

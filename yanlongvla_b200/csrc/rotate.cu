@@ -151,6 +151,97 @@ __global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, c
                    });
 }
 
+// The rotation op on power-of-two widths D = 2^NL (1024 .. 16384), one row per CTA of D / 32
+// threads. A thread holds 32 elements at a time, the ones whose index differs only in a 5-bit window of index bits
+// [lo, lo + 5); the butterfly stages of the window's bits run in registers (low slot a + b, high slot a - b, stages
+// in the order h = 1, 2, 4, ...: the definition's order, so the sums are bit-identical). Windows lo = 0, 5, and
+// NL - 5 cover all NL bits in increasing order (the last window repeats bits already done and applies only the new
+// ones); between windows the row passes through shared memory padded by one word per 32 (element e at e + e / 32),
+// where both the writes and the reads of every window are conflict-free and every address is the thread's base plus
+// an immediate. About 20 instructions per element (the general row kernel takes ~47).
+template <int NL>
+struct Win2 {
+    static constexpr int P = NL > 10 ? 3 : 2;                  // windows
+    static constexpr int lo(int p) { return p == 0 ? 0 : p == 1 ? 5 : NL - 5; }
+    static constexpr int first(int p) { return p == 0 ? 0 : p == 1 ? 5 : 10; }   // first index bit new in window p
+};
+
+__device__ __forceinline__ int pad32(int e) { return e + (e >> 5); }
+
+template <int DT, int OT, int NL>
+__global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
+                                                            void* __restrict__ y, int inverse) {
+    constexpr int D = 1 << NL;
+    using W = Win2<NL>;
+    extern __shared__ __align__(16) float buf[];
+    i8* ssg = reinterpret_cast<i8*>(buf + D + D / 32);             // inverse: the row's signs, for the strided output
+    pdl_launch_dependents();
+    const int t = threadIdx.x;
+    if (inverse) {                                                  // 32 signs per thread (read after a barrier below)
+        const uint4* src = reinterpret_cast<const uint4*>(sg) + 2 * t;
+        uint4* dst = reinterpret_cast<uint4*>(ssg) + 2 * t;
+        dst[0] = __ldg(src);
+        dst[1] = __ldg(src + 1);
+    }
+    pdl_wait();
+    const size_t row = blockIdx.x;
+    float v[32];
+    // window 0: 32 contiguous elements
+    {
+        const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+        loadc<DT, 32>(reinterpret_cast<const char*>(x) + (row * D + 32 * t) * es, v);
+        if (!inverse) {
+            float s32[32];
+            load_signsc<32, true>(sg + 32 * t, s32);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = v[k] * s32[k];
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < W::P; ++p) {
+        const int lo = W::lo(p);
+        const int base = ((t >> lo) << (lo + 5)) | (t & ((1 << lo) - 1));
+        if (p > 0) {
+#pragma unroll
+            for (int r = 0; r < 32; ++r) v[r] = buf[pad32(base) + r * ((1 << lo) + ((1 << lo) >> 5))];
+        }
+#pragma unroll
+        for (int sb = 0; sb < 5; ++sb) {
+            if (lo + sb < W::first(p)) continue;
+            const int hh = 1 << sb;
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+                if (!(k & hh)) {
+                    const float a = v[k], b = v[k + hh];
+                    v[k] = a + b;
+                    v[k + hh] = a - b;
+                }
+        }
+        if (p + 1 < W::P) {
+            if (p > 0) __syncthreads();                    // every thread has read window p before it is overwritten
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+                const int e = base + (r << lo);
+                buf[lo == 0 ? pad32(32 * t) + r : pad32(base) + r * ((1 << lo) + ((1 << lo) >> 5))] = v[r];
+                (void)e;
+            }
+            __syncthreads();
+        }
+    }
+    // the last window: scale, signs (inverse), store element base + (r << lo) of the row
+    const int lo = W::lo(W::P - 1);
+    const int base = ((t >> lo) << (lo + 5)) | (t & ((1 << lo) - 1));
+    const float sc = wscale(D);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+        const int e = base + (r << lo);
+        float o = v[r] * sc;
+        if (inverse) o = o * (float)ssg[e];
+        if (OT == TCQ_DT_F32) reinterpret_cast<float*>(y)[row * D + e] = o;
+        else reinterpret_cast<u16*>(y)[row * D + e] = f2bf(o);
+    }
+}
+
 // Epilogue of one layer on one token: SCALE(acc[base + i]) -> block Walsh -> * sv -> + bias -> BF16 (-> act).
 // out(i, b): one BF16 result; outc(i0, w): the CH results of chunk i0 as CH / 2 packed words (element i0 + k in the
 // low half of w[k / 2] for even k). sv / bias / rs may be shared-memory copies.
@@ -539,6 +630,27 @@ bool acc_aligned(const void* acc, int acc_dtype, int lda, int col0) {
 
 }  // namespace
 
+namespace {
+template <int NL>
+int launch_rotate_p2(const void* x, int x_dtype, const int8_t* signs, void* y, bool of, int M, int inv, void* stream) {
+    const size_t smem = (size_t)4 * ((1 << NL) + (1 << NL) / 32) + (1 << NL);
+    const int T = (1 << NL) / 32;
+    switch (x_dtype) {
+        case TCQ_DT_BF16:
+            return of ? launch(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
+                      : launch(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
+        case TCQ_DT_F16:
+            return of ? launch(k_rotate_p2<TCQ_DT_F16, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
+                      : launch(k_rotate_p2<TCQ_DT_F16, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
+        case TCQ_DT_F32:
+            return of ? launch(k_rotate_p2<TCQ_DT_F32, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
+                      : launch(k_rotate_p2<TCQ_DT_F32, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
+        default: return (int)TCQ_ERR_DTYPE;
+    }
+}
+
+}  // namespace
+
 extern "C" {
 
 int tcq_abi_version(void) { return TCQ_ABI_VERSION; }
@@ -632,6 +744,14 @@ int tcq_rotate(const void* x, int x_dtype, const int8_t* signs, void* y, int y_d
     if (y_dtype != TCQ_DT_F32 && y_dtype != TCQ_DT_BF16) return TCQ_ERR_DTYPE;
     if (!tcq_aligned(y, 16)) return TCQ_ERR_ALIGN;
     const bool of = y_dtype == TCQ_DT_F32;
+    switch (D) {                                           // power-of-two widths: the register-window kernel
+        case 1024: return launch_rotate_p2<10>(x, x_dtype, signs, y, of, M, inv, stream);
+        case 2048: return launch_rotate_p2<11>(x, x_dtype, signs, y, of, M, inv, stream);
+        case 4096: return launch_rotate_p2<12>(x, x_dtype, signs, y, of, M, inv, stream);
+        case 8192: return launch_rotate_p2<13>(x, x_dtype, signs, y, of, M, inv, stream);
+        case 16384: return launch_rotate_p2<14>(x, x_dtype, signs, y, of, M, inv, stream);
+        default: break;
+    }
     return with_ch(rows_ch(M, D, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
         const int T = threads_for(D, CH);

@@ -19,7 +19,8 @@ Product dispatch is per call, by token count M (the reference decides by model p
 the products, which all give the same bits:
   M <= SIMT_MAX_M                      SIMT products on q4 words: the fused trellis decode-GEMV, or the INT8-resident
                                        GEMV; FP32 scaled output
-  M <= TC_MAX_M, 2-bit stream          tcgen05 decode-GEMM with the trellis decode fused; FP32 scaled output
+  M <= TC_MAX_M, 2-bit stream          tcgen05 decode-GEMM with the trellis decode fused; FP32 scaled output (also up
+                                       to TC_WIDE_MAX_M tokens on products of at most TC_WIDE_MAX_TILES channel tiles)
   otherwise                            tcgen05 INT8 GEMM on resident INT8 weights, or on weights decoded just before
                                        into a temporary; INT32 accumulators, scaled by the post
 """
@@ -33,7 +34,9 @@ GROUPS = (('q_proj', 'k_proj', 'v_proj'), ('gate_proj', 'up_proj'))
 STATS = dict(group_runs=0, regroup_misses=0, fused_mlps=0)
 FUSE = dict(post3=True, mlp=True, split=True, chain=True, pre_gemv=True)
 SIMT_MAX_M = 4
-TC_MAX_M = 32
+TC_MAX_M = 32               # 2-bit stream: the tensor-core decode-GEMM for up to this many tokens,
+TC_WIDE_MAX_M = 160         # and for up to this many when the product has at most TC_WIDE_MAX_TILES 128-channel tiles
+TC_WIDE_MAX_TILES = 24      # (enough K splits per tile to spread the decode over the SMs)
 FLOAT_MAX_M = 16            # W2 float path: fused FP32 products up to this many tokens, BF16 GEMM above
 _NO_BOUND = 1 << 30         # layer-boundary slot of a group with fewer than three members
 
@@ -155,7 +158,8 @@ class Group:
                 K.gemm_w8(self.W, q4, b['scale'], self.rs, z)
             return z
         q = b['q']
-        if self.W is None and self.tc_ok and q.shape[0] <= TC_MAX_M:
+        M = q.shape[0]
+        if self.W is None and self.tc_ok and (M <= TC_MAX_M or (M <= TC_WIDE_MAX_M and -(-self.Ntot // 128) <= TC_WIDE_MAX_TILES)):
             z = self._fp32_out(q.shape[0], q.device)
             K.gemm_tcq_tc(self.bits, self.t8, q, b['scale'], self.rs, z, self.K, self.bounds)
             return z
