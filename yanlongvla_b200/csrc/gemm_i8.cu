@@ -766,7 +766,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             u32 peer[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) peer[r] = r < R ? (P.cl ? map_to_rank(smem_u32(smem), r) : smem_u32(smem)) : 0u;
-            constexpr int NT = 32 * kTcDecWarps, U = 8;
+            constexpr int NT = 32 * kTcDecWarps, U = 4;
             for (int g0 = (int)((long long)G * rank / R) + (int)threadIdx.x - 64; g0 < g_end; g0 += U * NT) {
                 int4 sum[U];
 #pragma unroll

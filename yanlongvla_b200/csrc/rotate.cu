@@ -152,21 +152,20 @@ __global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, c
 }
 
 // The rotation op on power-of-two widths D = 2^NL (1024 .. 16384), one row per CTA of D / 32
-// threads. A thread holds 32 elements at a time, the ones whose index differs only in a 5-bit window of index bits
-// [lo, lo + 5); the butterfly stages of the window's bits run in registers (low slot a + b, high slot a - b, stages
-// in the order h = 1, 2, 4, ...: the definition's order, so the sums are bit-identical). Windows lo = 0, 5, and
-// NL - 5 cover all NL bits in increasing order (the last window repeats bits already done and applies only the new
-// ones); between windows the row passes through shared memory padded by one word per 32 (element e at e + e / 32),
-// where both the writes and the reads of every window are conflict-free and every address is the thread's base plus
-// an immediate. About 20 instructions per element (the general row kernel takes ~47).
+// threads. A thread holds 32 elements at a time: 4 consecutive ones (index bits 0, 1) times the 8 values of a 3-bit
+// window of index bits [lo, lo + 3) (the first window is bits 0..4, i.e. 32 consecutive elements). The butterfly
+// stages of the window's new bits run in registers (low slot a + b, high slot a - b, in the order h = 1, 2, 4, ...:
+// the definition's order, so the sums are bit-identical). Windows after the first take 3 new bits each in
+// increasing order (the last one slides down to end at bit NL - 1 and skips bits already done). Between windows the
+// row passes through shared memory as 16-byte groups, padded by 16 bytes per 128 (group g at g + g / 8): every
+// access of every window is a conflict-free 16-byte one, at the thread's base plus an immediate. The last window
+// stores 4 consecutive outputs at a time.
 template <int NL>
 struct Win2 {
-    static constexpr int P = NL > 10 ? 3 : 2;                  // windows
-    static constexpr int lo(int p) { return p == 0 ? 0 : p == 1 ? 5 : NL - 5; }
-    static constexpr int first(int p) { return p == 0 ? 0 : p == 1 ? 5 : 10; }   // first index bit new in window p
+    static constexpr int P = 1 + (NL - 5 + 2) / 3;                         // windows
+    static constexpr int first(int p) { return p == 0 ? 0 : 5 + 3 * (p - 1); }   // first index bit new in window p
+    static constexpr int lo(int p) { return p == 0 ? 2 : (first(p) + 3 <= NL ? first(p) : NL - 3); }
 };
-
-__device__ __forceinline__ int pad32(int e) { return e + (e >> 5); }
 
 template <int DT, int OT, int NL>
 __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
@@ -174,7 +173,8 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
     constexpr int D = 1 << NL;
     using W = Win2<NL>;
     extern __shared__ __align__(16) float buf[];
-    i8* ssg = reinterpret_cast<i8*>(buf + D + D / 32);             // inverse: the row's signs, for the strided output
+    float4* b4 = reinterpret_cast<float4*>(buf);
+    i8* ssg = reinterpret_cast<i8*>(buf + D + D / 8);               // inverse: the row's signs, for the last window
     pdl_launch_dependents();
     const int t = threadIdx.x;
     if (inverse) {                                                  // 32 signs per thread (read after a barrier below)
@@ -186,7 +186,6 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
     pdl_wait();
     const size_t row = blockIdx.x;
     float v[32];
-    // window 0: 32 contiguous elements
     {
         const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
         loadc<DT, 32>(reinterpret_cast<const char*>(x) + (row * D + 32 * t) * es, v);
@@ -197,17 +196,24 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
             for (int k = 0; k < 32; ++k) v[k] = v[k] * s32[k];
         }
     }
+    // element of register r in window p: (r & 3) | thread bits at 2 .. lo - 1 | (r >> 2) << lo | thread bits >= lo + 3
+    auto ebase = [&](int lo) { return ((t & ((1 << (lo - 2)) - 1)) << 2) | ((t >> (lo - 2)) << (lo + 3)); };
 #pragma unroll
     for (int p = 0; p < W::P; ++p) {
         const int lo = W::lo(p);
-        const int base = ((t >> lo) << (lo + 5)) | (t & ((1 << lo) - 1));
+        const int g0 = ebase(lo) >> 2, ph0 = g0 + (g0 >> 3);          // padded 16-byte group of register group 0
+        const int gstep = (1 << (lo - 2)) + (lo >= 5 ? (1 << (lo - 5)) : 0);   // padded step between register groups
         if (p > 0) {
 #pragma unroll
-            for (int r = 0; r < 32; ++r) v[r] = buf[pad32(base) + r * ((1 << lo) + ((1 << lo) >> 5))];
+            for (int q = 0; q < 8; ++q) {
+                const float4 a = b4[ph0 + q * gstep];
+                v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+            }
         }
 #pragma unroll
         for (int sb = 0; sb < 5; ++sb) {
-            if (lo + sb < W::first(p)) continue;
+            const int bit = sb < 2 ? sb : lo + sb - 2;
+            if (bit < W::first(p) || (p > 0 && sb < 2)) continue;
             const int hh = 1 << sb;
 #pragma unroll
             for (int k = 0; k < 32; ++k)
@@ -220,25 +226,30 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
         if (p + 1 < W::P) {
             if (p > 0) __syncthreads();                    // every thread has read window p before it is overwritten
 #pragma unroll
-            for (int r = 0; r < 32; ++r) {
-                const int e = base + (r << lo);
-                buf[lo == 0 ? pad32(32 * t) + r : pad32(base) + r * ((1 << lo) + ((1 << lo) >> 5))] = v[r];
-                (void)e;
-            }
+            for (int q = 0; q < 8; ++q) b4[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             __syncthreads();
         }
     }
-    // the last window: scale, signs (inverse), store element base + (r << lo) of the row
-    const int lo = W::lo(W::P - 1);
-    const int base = ((t >> lo) << (lo + 5)) | (t & ((1 << lo) - 1));
+    // the last window: scale, signs (inverse), 4 consecutive outputs per store
+    constexpr int LO = W::lo(W::P - 1);
+    const int e0 = ebase(LO);
     const float sc = wscale(D);
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-        const int e = base + (r << lo);
-        float o = v[r] * sc;
-        if (inverse) o = o * (float)ssg[e];
-        if (OT == TCQ_DT_F32) reinterpret_cast<float*>(y)[row * D + e] = o;
-        else reinterpret_cast<u16*>(y)[row * D + e] = f2bf(o);
+    for (int q = 0; q < 8; ++q) {
+        const int e = e0 + (q << LO);
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = v[4 * q + k] * sc;
+        if (inverse) {
+            const u32 sw = *reinterpret_cast<const u32*>(ssg + e);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o[k] = o[k] * (float)(i8)((sw >> (8 * k)) & 0xffu);
+        }
+        if (OT == TCQ_DT_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D + e) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+            *reinterpret_cast<uint2*>(reinterpret_cast<u16*>(y) + row * D + e) = make_uint2(f2bf2(o[0], o[1]), f2bf2(o[2], o[3]));
+        }
     }
 }
 
@@ -633,18 +644,13 @@ bool acc_aligned(const void* acc, int acc_dtype, int lda, int col0) {
 namespace {
 template <int NL>
 int launch_rotate_p2(const void* x, int x_dtype, const int8_t* signs, void* y, bool of, int M, int inv, void* stream) {
-    const size_t smem = (size_t)4 * ((1 << NL) + (1 << NL) / 32) + (1 << NL);
+    const size_t smem = (size_t)4 * ((1 << NL) + (1 << NL) / 8) + (1 << NL);
     const int T = (1 << NL) / 32;
+    auto go = [&](auto kern) { return launch(kern, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv); };
     switch (x_dtype) {
-        case TCQ_DT_BF16:
-            return of ? launch(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
-                      : launch(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
-        case TCQ_DT_F16:
-            return of ? launch(k_rotate_p2<TCQ_DT_F16, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
-                      : launch(k_rotate_p2<TCQ_DT_F16, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
-        case TCQ_DT_F32:
-            return of ? launch(k_rotate_p2<TCQ_DT_F32, TCQ_DT_F32, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv)
-                      : launch(k_rotate_p2<TCQ_DT_F32, TCQ_DT_BF16, NL>, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv);
+        case TCQ_DT_BF16: return of ? go(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_F32, NL>) : go(k_rotate_p2<TCQ_DT_BF16, TCQ_DT_BF16, NL>);
+        case TCQ_DT_F16: return of ? go(k_rotate_p2<TCQ_DT_F16, TCQ_DT_F32, NL>) : go(k_rotate_p2<TCQ_DT_F16, TCQ_DT_BF16, NL>);
+        case TCQ_DT_F32: return of ? go(k_rotate_p2<TCQ_DT_F32, TCQ_DT_F32, NL>) : go(k_rotate_p2<TCQ_DT_F32, TCQ_DT_BF16, NL>);
         default: return (int)TCQ_ERR_DTYPE;
     }
 }
