@@ -98,7 +98,8 @@ def test_gemm_tcq_every_m(K, M):
     _eq(n(z2), zr, f'gemm_w8 M={M}')
 
 
-@pytest.mark.parametrize('M,N,Kd', [(1, 4096, 4096), (3, 2048, 8192), (10, 1536, 6144), (16, 512, 16384), (2, 6144, 1152)])
+@pytest.mark.parametrize('M,N,Kd', [(1, 4096, 4096), (3, 2048, 8192), (10, 1536, 6144), (16, 512, 16384), (2, 6144, 1152),
+                                    (1, 4112, 4080), (1, 2048, 8192), (1, 8192, 2048)])
 def test_gemm_tcq_shapes(K, M, N, Kd):
     """Stream-K split across warps / CTAs at policy shapes; repeated calls keep the workspace clean."""
     L = DevLayer(f'shape{N}x{Kd}', N, Kd, False)
@@ -110,6 +111,23 @@ def test_gemm_tcq_shapes(K, M, N, Kd):
         z.zero_()
         K.gemm_tcq(L.bits, L.t8, t(O.q4_words(q)), t(s), L.rs, z, Kd)
         _eq(n(z), zr, f'gemm_tcq {M}x{N}x{Kd}')
+
+
+def test_gemm_tcq_one_token_unaligned_activations(K):
+    """M = 1 with activation words that do not start on a 16-byte boundary (scalar activation loads), on a layer large
+    enough for one lane per tile whose last unit of each tile row is partial (4112 x 4080)."""
+    L = DevLayer('g1u4112x4080', 4112, 4080, False)
+    x = cases.activations('g1u4112x4080', 1, 4080, 'bf16')
+    q, s = O.pre(x, 'bf16', L.ref.su)
+    zr = O.gemm_z(q, L.ref.w8_reference(), s, L.ref.rs)
+    words = t(O.q4_words(q))
+    buf = torch.zeros(words.numel() + 1, dtype=torch.int32, device='cuda')
+    buf[1:] = words.reshape(-1)
+    q4 = buf[1:].view(words.shape)
+    assert q4.data_ptr() % 16 != 0
+    z = torch.empty(1, 4112, dtype=torch.float32, device='cuda')
+    K.gemm_tcq(L.bits, L.t8, q4, t(s), L.rs, z, 4080)
+    _eq(n(z), zr, 'gemm_tcq one token, unaligned activations')
 
 
 @pytest.mark.parametrize('M,N,Kd,dt', [(1, 4096, 4096, 'bf16'), (1, 512, 1152, 'f16'), (2, 2048, 8192, 'f32'),

@@ -1019,14 +1019,16 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     P.ct = (N + BM - 1) / BM;
     P.kb = (K + BK - 1) / BK;
     // K splits: the splits of a channel tile form a cluster (at most 8, a portable size) that reduces in distributed
-    // shared memory, each rank finishing one slice of the tile: the largest split with at least 3 K stages per CTA
-    // (2 for token tiles wider than 32) whose clusters are all resident at once (one CTA fills an SM, so clusters pack
-    // into the GPCs only so far). When no cluster of 2 or more fits, the splits reduce through workspace slices (at
-    // most kTcKsMax).
+    // shared memory, each rank finishing one slice of the tile: the largest split whose clusters are all resident at
+    // once (one CTA fills an SM, so clusters pack into the GPCs only so far), with about 4 K stages per CTA for 32-token
+    // tiles from 12 stages on (measured at 17 tokens: 4 splits beat 6 and 8 at 12 and 16 stages, 8 beat 6 at 48), at
+    // least 3 below that, and at least 2 for wider token tiles. When no cluster of 2 or more fits, the splits reduce
+    // through workspace slices (at most kTcKsMax).
     int ks = 1;
     bool cl = false;
     {
-        int c = std::min({8, sms() / P.ct, P.kb, BN == 32 ? (P.kb + 2) / 3 : P.kb / 2});
+        const int want = BN == 32 ? (P.kb >= 12 ? std::max(4, (P.kb + 3) / 4) : (P.kb + 2) / 3) : P.kb / 2;
+        int c = std::min({8, sms() / P.ct, P.kb, want});
         for (; c >= 2; --c)
             if (P.ct <= max_clusters(kern, smem, c)) break;
         if (c >= 2) {

@@ -69,22 +69,26 @@ __device__ __forceinline__ void build_table_bf16(u32* tab, u32* pairs, const u16
     }
 }
 
-// Table lookup of this lane's copy: byte offset (key * 128) | (4 * lane) from the shared table `tab` (the key offset
-// has bits 7..16, the lane offset bits 2..6, so one OR joins them; the constant shared base is added by the compiler).
-__device__ __forceinline__ u32 lut(const u32* tab, u32 lane4, u32 off) {
-    return *reinterpret_cast<const u32*>(reinterpret_cast<const char*>(tab) + (off | lane4));
+// Table lookup of this lane's copy: byte offset (key * 128) | (4 * lane) from the shared table `tab`: the key offset
+// is bits 7..16 of t (below), the lane offset bits 2..6, so one three-input logic op (t & 0x1FF80) | lane4 forms the
+// address (written as one lop3 so that the mask and the lane always fuse); the constant shared base is added by the
+// compiler.
+__device__ __forceinline__ u32 lut(const u32* tab, u32 lane4, u32 t) {
+    u32 off;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(off) : "r"(t), "n"(0x1FF80), "r"(lane4));   // (a & b) | c
+    return *reinterpret_cast<const u32*>(reinterpret_cast<const char*>(tab) + off);
 }
 
-// Byte offset key * 128 of the state in the upper half of F: v = F >> 16 taken as the high word of F * 2^16 (multiply
-// pipe), 2x = v * 2v + 2v, bits 7..16 of 2x = bits 6..15 of x = key.
+// 2x for the state in the upper half of F: v = F >> 16 taken as the high word of F * 2^16 (multiply pipe),
+// 2x = v * 2v + 2v; bits 7..16 of 2x = bits 6..15 of x = key.
 __device__ __forceinline__ u32 off_hi(u32 F) {
     const u32 v = __umulhi(F, 65536u), u = v * 2u;
-    return (v * u + u) & 0x1FF80u;
+    return v * u + u;
 }
-// Byte offset of the state in the lower half of F (bits above 16 are junk and drop out of bits 7..16 of 2x).
+// 2x for the state in the lower half of F (bits above 16 are junk and drop out of bits 7..16 of 2x).
 __device__ __forceinline__ u32 off_lo(u32 F) {
     const u32 u = F * 2u;
-    return (F * u + u) & 0x1FF80u;
+    return F * u + u;
 }
 
 // The 8 table entries of one tile row. A = (w[2r] << 16) | w[2r+1], B = (w[2r+2] << 16) | w[2r+3] (words mod 32):
