@@ -152,29 +152,41 @@ __global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, c
 }
 
 // The rotation op on power-of-two widths D = 2^NL (1024 .. 16384), one row per CTA of D / 32
-// threads. A thread holds 32 elements at a time: 4 consecutive ones (index bits 0, 1) times the 8 values of a 3-bit
-// window of index bits [lo, lo + 3) (the first window is bits 0..4, i.e. 32 consecutive elements). The butterfly
-// stages of the window's new bits run in registers (low slot a + b, high slot a - b, in the order h = 1, 2, 4, ...:
-// the definition's order, so the sums are bit-identical). Windows after the first take 3 new bits each in
-// increasing order (the last one slides down to end at bit NL - 1 and skips bits already done). Between windows the
-// row passes through shared memory as 16-byte groups, padded by 16 bytes per 128 (group g at g + g / 8): every
-// access of every window is a conflict-free 16-byte one, at the thread's base plus an immediate. The last window
-// stores 4 consecutive outputs at a time.
-template <int NL>
+// threads. A thread holds 32 elements at a time: V consecutive ones (index bits 0 .. log2 V - 1) times the 2^WB values
+// of a WB-bit window of index bits [lo, lo + WB), WB = 5 - log2 V (the first window is bits 0..4, i.e. 32 consecutive
+// elements). The butterfly stages of the window's new bits run in registers (low slot a + b, high slot a - b, in the
+// order h = 1, 2, 4, ...: the definition's order, so the sums are bit-identical). Windows after the first take WB new
+// bits each in increasing order (the last one slides down to end at bit NL - 1 and skips bits already done). Between
+// windows the row passes through shared memory as groups of V floats, with one group of padding after every 2^WB
+// groups (group g at g + g / 2^WB): window 0's threads start 2^WB + 1 groups apart and every later window has
+// lo - log2 V >= WB, so every access of every window is conflict-free (16 lanes per 128-byte phase for V = 2, 8 for
+// V = 4), at the thread's base plus an immediate. The last window stores V consecutive outputs at a time.
+// V = 2 (WB = 4) takes two exchanges at D = 4096 and 8192 where V = 4 (WB = 3) takes three (16 instead of 24 bytes
+// of shared-memory traffic per element: 4096 x 4096 in 20.0 instead of 23.0 us), and at 16384 three either way but
+// wins 2 % there; at 1024 and 2048 the counts are equal and V = 4 moves them with half the instructions.
+template <int NL, int V>
 struct Win2 {
-    static constexpr int P = 1 + (NL - 5 + 2) / 3;                         // windows
-    static constexpr int first(int p) { return p == 0 ? 0 : 5 + 3 * (p - 1); }   // first index bit new in window p
-    static constexpr int lo(int p) { return p == 0 ? 2 : (first(p) + 3 <= NL ? first(p) : NL - 3); }
+    static_assert(V == 2 || V == 4, "exchange vectors of 2 or 4 floats");
+    static constexpr int VB = V == 2 ? 1 : 2, WB = 5 - VB;
+    static constexpr int P = 1 + (NL - 5 + WB - 1) / WB;                                 // windows
+    static constexpr int first(int p) { return p == 0 ? 0 : 5 + WB * (p - 1); }        // first index bit new in window p
+    static constexpr int lo(int p) { return p == 0 ? VB : (first(p) + WB <= NL ? first(p) : NL - WB); }
 };
+
+template <int NL>
+constexpr int rot_vec() { return NL >= 12 ? 2 : 4; }
 
 template <int DT, int OT, int NL>
 __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
                                                             void* __restrict__ y, int inverse) {
-    constexpr int D = 1 << NL;
-    using W = Win2<NL>;
+    constexpr int D = 1 << NL, V = rot_vec<NL>();
+    using W = Win2<NL, V>;
+    constexpr int VB = W::VB, WB = W::WB, G = 1 << WB;
+    static_assert(NL >= 2 * WB + VB, "every window after the first needs lo - log2 V >= WB");
+    using VecT = typename std::conditional<V == 2, float2, float4>::type;
     extern __shared__ __align__(16) float buf[];
-    float4* b4 = reinterpret_cast<float4*>(buf);
-    i8* ssg = reinterpret_cast<i8*>(buf + D + D / 8);               // inverse: the row's signs, for the last window
+    VecT* bv = reinterpret_cast<VecT*>(buf);
+    i8* ssg = reinterpret_cast<i8*>(buf + D + (D >> WB));          // inverse: the row's signs, for the last window
     pdl_launch_dependents();
     const int t = threadIdx.x;
     if (inverse) {                                                  // 32 signs per thread (read after a barrier below)
@@ -196,24 +208,29 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
             for (int k = 0; k < 32; ++k) v[k] = v[k] * s32[k];
         }
     }
-    // element of register r in window p: (r & 3) | thread bits at 2 .. lo - 1 | (r >> 2) << lo | thread bits >= lo + 3
-    auto ebase = [&](int lo) { return ((t & ((1 << (lo - 2)) - 1)) << 2) | ((t >> (lo - 2)) << (lo + 3)); };
+    // element of register r in window p: (r % V) | thread bits at VB .. lo - 1 | (r / V) << lo | thread bits >= lo + WB
+    auto ebase = [&](int lo) { return ((t & ((1 << (lo - VB)) - 1)) << VB) | ((t >> (lo - VB)) << (lo + WB)); };
 #pragma unroll
     for (int p = 0; p < W::P; ++p) {
         const int lo = W::lo(p);
-        const int g0 = ebase(lo) >> 2, ph0 = g0 + (g0 >> 3);          // padded 16-byte group of register group 0
-        const int gstep = (1 << (lo - 2)) + (lo >= 5 ? (1 << (lo - 5)) : 0);   // padded step between register groups
+        const int g0 = ebase(lo) >> VB, ph0 = g0 + (g0 >> WB);       // padded group of register group 0
+        // padded step between register groups (window 0: consecutive groups within one padding period)
+        const int gstep = p == 0 ? 1 : (1 << (lo - VB)) + (1 << (lo - VB - WB));
         if (p > 0) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 a = b4[ph0 + q * gstep];
-                v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+            for (int q = 0; q < G; ++q) {
+                const VecT a = bv[ph0 + q * gstep];
+                if constexpr (V == 2) {
+                    v[2 * q] = a.x; v[2 * q + 1] = a.y;
+                } else {
+                    v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+                }
             }
         }
 #pragma unroll
         for (int sb = 0; sb < 5; ++sb) {
-            const int bit = sb < 2 ? sb : lo + sb - 2;
-            if (bit < W::first(p) || (p > 0 && sb < 2)) continue;
+            const int bit = sb < VB ? sb : lo + sb - VB;
+            if (bit < W::first(p) || (p > 0 && sb < VB)) continue;
             const int hh = 1 << sb;
 #pragma unroll
             for (int k = 0; k < 32; ++k)
@@ -226,29 +243,37 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
         if (p + 1 < W::P) {
             if (p > 0) __syncthreads();                    // every thread has read window p before it is overwritten
 #pragma unroll
-            for (int q = 0; q < 8; ++q) b4[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int q = 0; q < G; ++q) {
+                if constexpr (V == 2) bv[ph0 + q * gstep] = make_float2(v[2 * q], v[2 * q + 1]);
+                else bv[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
             __syncthreads();
         }
     }
-    // the last window: scale, signs (inverse), 4 consecutive outputs per store
+    // the last window: scale, signs (inverse), V consecutive outputs per store
     constexpr int LO = W::lo(W::P - 1);
     const int e0 = ebase(LO);
     const float sc = wscale(D);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < G; ++q) {
         const int e = e0 + (q << LO);
-        float o[4];
+        float o[V];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) o[k] = v[4 * q + k] * sc;
+        for (int k = 0; k < V; ++k) o[k] = v[V * q + k] * sc;
         if (inverse) {
-            const u32 sw = *reinterpret_cast<const u32*>(ssg + e);
+            const u32 sw = V == 2 ? (u32)*reinterpret_cast<const u16*>(ssg + e) : *reinterpret_cast<const u32*>(ssg + e);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) o[k] = o[k] * (float)(i8)((sw >> (8 * k)) & 0xffu);
+            for (int k = 0; k < V; ++k) o[k] = o[k] * (float)(i8)((sw >> (8 * k)) & 0xffu);
         }
-        if (OT == TCQ_DT_F32) {
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D + e) = make_float4(o[0], o[1], o[2], o[3]);
+        if constexpr (V == 2) {
+            if (OT == TCQ_DT_F32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(y) + row * D + e) = make_float2(o[0], o[1]);
+            else *reinterpret_cast<u32*>(reinterpret_cast<u16*>(y) + row * D + e) = f2bf2(o[0], o[1]);
         } else {
-            *reinterpret_cast<uint2*>(reinterpret_cast<u16*>(y) + row * D + e) = make_uint2(f2bf2(o[0], o[1]), f2bf2(o[2], o[3]));
+            if (OT == TCQ_DT_F32) {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * D + e) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+                *reinterpret_cast<uint2*>(reinterpret_cast<u16*>(y) + row * D + e) = make_uint2(f2bf2(o[0], o[1]), f2bf2(o[2], o[3]));
+            }
         }
     }
 }
@@ -644,7 +669,8 @@ bool acc_aligned(const void* acc, int acc_dtype, int lda, int col0) {
 namespace {
 template <int NL>
 int launch_rotate_p2(const void* x, int x_dtype, const int8_t* signs, void* y, bool of, int M, int inv, void* stream) {
-    const size_t smem = (size_t)4 * ((1 << NL) + (1 << NL) / 8) + (1 << NL);
+    constexpr int WB = Win2<NL, rot_vec<NL>()>::WB;
+    const size_t smem = (size_t)4 * ((1 << NL) + ((1 << NL) >> WB)) + (1 << NL);
     const int T = (1 << NL) / 32;
     auto go = [&](auto kern) { return launch(kern, dim3(M), T, smem, stream, x, (const i8*)signs, y, inv); };
     switch (x_dtype) {
