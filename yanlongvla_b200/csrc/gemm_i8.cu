@@ -637,9 +637,13 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
     __syncthreads();
     tc_fence_after();
     const u32 tmem = *tmem_slot;
-    pdl_wait();
+    // The dependency wait is per role: the token tiles (TMA) and everything the epilogue reads or writes in global
+    // memory come after it; the decoders run ahead of it through the first STAGES K stages (the weights and the table
+    // are layer constants), so a launch that starts while its predecessor runs has its first stages decoded by the
+    // time the activations are ready. The MMA issuer touches only shared memory and TMEM.
 
     if (warp == 0) {
+        pdl_wait();
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmQ) : "memory");
             int st = 0;
@@ -669,6 +673,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             (void)ok;
             mma_commit(tfull);   // also on an early stop: it arrives once every MMA issued so far has finished
         }
+        pdl_wait();
     } else {
         // ---- decoders (tile (di, dj), tile rows 2 dg, 2 dg + 1 of each stage; see load_words)
         const int i = di, j = dj, g = dg;
@@ -700,6 +705,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             if (lane == 0) mbar_arrive(full0 + 8 * st);
             if (++st == STAGES) { st = 0; ph ^= 1; }
         }
+        pdl_wait();                                  // the epilogue reads the token scales and writes z / the workspace
         // ---- epilogue
         if (P.ks == 1 || P.cl) {
             // Every decoder warp moves part of the accumulator from TMEM (its lane quarter warp & 3, column groups

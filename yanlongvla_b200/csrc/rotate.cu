@@ -308,7 +308,7 @@ __device__ __forceinline__ void post_row(float* buf, const void* acc, size_t bas
 }
 
 template <int AT, int CH>
-__global__ void __launch_bounds__(512, 1) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+__global__ void __launch_bounds__(512, 2) k_post(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, u16* __restrict__ y, int M,
                                               int N, int lda, int col0, int stage) {
     extern __shared__ __align__(16) float buf[];
@@ -507,7 +507,7 @@ __device__ __forceinline__ void buf_chunk(const float* buf, int c, float* v) {
 // Gated-MLP middle (kernels.py:263-278): g = lut(BF16(post(gate))), u = BF16(post(up)), x = BF16(g * u) * su,
 // block Walsh, INT8. Shared memory: N floats + N BF16.
 template <int AT, int CH>
-__global__ void __launch_bounds__(512, 1) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+__global__ void __launch_bounds__(512, 2) k_mid2(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const u16* __restrict__ lut, const i8* __restrict__ su,
                                               int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale, int M, int N,
                                               int lda, int ldq, int stage) {
@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(512, 1) k_mid2(const void* __restrict__ acc, c
 
 // Plain-MLP middle (kernels.py:280-292): x = lut(BF16(post(acc) + bias)) * su, block Walsh, INT8.
 template <int AT, int CH>
-__global__ void __launch_bounds__(512, 1) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
+__global__ void __launch_bounds__(512, 2) k_mid1(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs,
                                               const i8* __restrict__ sv, const float* __restrict__ bias, const u16* __restrict__ lut,
                                               const i8* __restrict__ su, int8_t* __restrict__ q, int* __restrict__ q4,
                                               float* __restrict__ scale, int M, int N, int lda, int ldq, int stage) {
@@ -621,8 +621,8 @@ int threads_for(int K, int CH) {
 int rows_ch(int M, int K, int per_sm) {
     return (long long)M * threads_for(K, 4) <= (long long)tcq_sm_count() * per_sm ? 4 : 16;
 }
-constexpr int kLightPerSm = 1024;   // row kernels of few registers (pre, rotate)
-constexpr int kHeavyPerSm = 512;    // row kernels with the epilogue's operands in registers (post, middles, chain)
+constexpr int kLightPerSm = 1024;   // row kernels of at most 64 registers a thread (pre, rotate, post, middles)
+constexpr int kHeavyPerSm = 512;    // row kernels with the epilogue's operands in registers (chain, post_multi)
 
 // Threads per row of the heavy row kernels (80-96 registers a thread: one 512-thread block fills an SM's register
 // file): more rows than SMs get at most 256 threads a row (two chunks a thread on the widest rows), so that two rows
@@ -813,9 +813,9 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
-    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+    return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = heavy_threads(M, N, CH);
+        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
             case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
@@ -925,9 +925,9 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 8 * N : 0) + 2 * N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)6 * N + (st ? cb : 0);
-    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+    return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = heavy_threads(M, N, CH);
+        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
@@ -951,9 +951,9 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
-    return with_ch(rows_ch(M, N, kHeavyPerSm), [&](auto C) {
+    return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = heavy_threads(M, N, CH);
+        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
