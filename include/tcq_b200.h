@@ -12,9 +12,11 @@
  *     any stream capture;
  *   - `stream` is a cudaStream_t (NULL = the legacy default stream);
  *   - kernels are launched with programmatic dependent launch and read a layer's constants (the packed trellis
- *     stream `bits`, its table `t8`, row scales, sign vectors, norm weights) before waiting for the kernel queued
+ *     stream `bits`, its table `t8`, row scales, sign vectors, norm weights) before waiting for the work queued
  *     before them on the stream; everything else (activations, accumulators, token scales, outputs) only after. A
- *     layer's constants must therefore not be written by the immediately preceding kernel in the same stream;
+ *     kernel launched the ordinary way completes before the next launch starts, so it may write those constants;
+ *     a writer that itself releases its dependents early (griddepcontrol.launch_dependents) needs an event wait or
+ *     a stream synchronization before the call;
  *   - optional outputs / inputs may be NULL where stated (the reference passes None for them, cuda_rt.py:90-91);
  *   - BF16 values are passed as uint16_t bit patterns; dtype codes are TCQ_DT_*;
  *   - the return value is a tcq_status: 0 on success; shapes and alignment are validated on the host before any
