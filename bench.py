@@ -1,8 +1,8 @@
-"""Benchmark of the fused 2-bit trellis decode-GEMV (BASELINE metric) on B200.
+"""Benchmark of the fused 2-bit trellis decode-GEMV (the benchmark metric) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
-Workload (BASELINE config 1 at its own shape): L = 64 distinct 4096 x 4096 trellis-coded layers (2 bits / weight,
+Workload (benchmark config 1 at its own shape): L = 64 distinct 4096 x 4096 trellis-coded layers (2 bits / weight,
 L = 16 bitshift trellis, 16 x 16 tiles, 512 x 2 table, seeded synthetic streams) -> 256 MiB of 2-bit stream per step,
 twice the 126 MB L2, so every step streams the weights from HBM (no L2 flush needed). One step = the decode-GEMV of
 every layer on its own token (M = 1), one launch per layer, captured in one CUDA graph with programmatic dependent

@@ -63,7 +63,7 @@ int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4
             int M, int K, int ldq, void* stream);
 
 /* The per-token INT8 quantizer alone, without rotation (tcq_format.quantize_tokens, tcq_format.py:119-122), for
- * W8A8 layers that are not rotated (the vision tower): x (M, K) BF16/F16/F32 -> q (M, K) int8,
+ * W8A8 layers that are not rotated (benchmark config 3, the vision tower): x (M, K) BF16/F16/F32 -> q (M, K) int8,
  * scale (M,) float32 = absmax / 127 (1 for an all-zero row). */
 int tcq_quantize(const void* x, int x_dtype, int8_t* q, float* scale, int M, int K, void* stream);
 
@@ -163,7 +163,7 @@ size_t tcq_gemm_tcq_noalloc_max_elements(void);
  * acc (M, N) int32 = q W^T, exact. */
 int tcq_int_mm(const int8_t* q, const int8_t* W, int32_t* acc, int M, int N, int K, void* stream);
 
-/* The reference's product + scale epilogue in one launch (tcq_format.py:135):
+/* The reference's product + scale epilogue in one launch (tcq_format.py:135; benchmark config 3):
  * out (M, N) = ((float)acc * s_tok[t]) * s_ch[n] as BF16 (out_dtype TCQ_DT_BF16) or FP32 (TCQ_DT_F32). */
 int tcq_int8_gemm(const int8_t* q, const int8_t* W, const float* s_tok, const float* s_ch, void* out, int out_dtype,
                   int M, int N, int K, void* stream);

@@ -17,7 +17,7 @@ LAYERS = [
     ('vit_in', 64, 1152, (3, 20), 'bf16', True),       # 1152 = 1024 + 128
     ('vit_fc2', 32, 4304, (2,), 'f32', False),         # 4304 = 4096 + 128 + 64 + 16
     ('dit', 1536, 1536, (1, 10), 'bf16', False),       # 1536 = 1024 + 512
-    ('config1', 4096, 4096, (1,), 'f16', False),
+    ('config1', 4096, 4096, (1,), 'f16', False),       # benchmark config 1
 ]
 
 # (T, D) for the standalone rotation (config 2 widths; T kept small for the CPU reference)

@@ -1,4 +1,4 @@
-"""Parity at the BASELINE configurations' full sizes, where the float64 oracle would take minutes: exact,
+"""Parity at the benchmark configurations' full sizes, where the float64 oracle would take minutes: exact,
 size-independent properties plus oracle checks on sampled rows.
 
 - config 3 (W8A8 GEMM), every M x (K, N) of the grid: the INT32 accumulator satisfies acc r = q (W^T r) exactly in

@@ -68,7 +68,7 @@ def test_int_mm_extremes(K):
 
 @pytest.mark.parametrize('M,Kd,N', cases.GEMMS)
 def test_int8_gemm_config3_golden(K, M, Kd, N):
-    """BASELINE config 3 end to end: per-token quantizer kernel + tcgen05 GEMM + scale epilogue == the reference."""
+    """benchmark config 3 end to end: per-token quantizer kernel + tcgen05 GEMM + scale epilogue == the reference."""
     a, w, sc = cases.gemm_inputs(M, Kd, N)
     qd, sd = K.quantize(t(a, 'bf16'))
     golden.check(f'gemm/{M}x{Kd}x{N}/q', n(qd))

@@ -323,7 +323,7 @@ def test_post3(K, M):
 
 
 def test_config1_fused_linear(K):
-    """4096 x 4096 layer, x fp16 [1, 4096]: pre -> fused decode-GEMV -> post == reference y."""
+    """benchmark config 1: 4096 x 4096 layer, x fp16 [1, 4096]: pre -> fused decode-GEMV -> post == reference y."""
     L = DevLayer('config1', 4096, 4096, False)
     x = cases.activations('config1', 1, 4096, 'f16')
     q4 = torch.empty(1024, 1, dtype=torch.int32, device='cuda')

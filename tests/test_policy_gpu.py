@@ -1,4 +1,4 @@
-"""The GR00T-style quantized policy (BASELINE configs 4 and 5) at reduced depth, against its 'reference' runtime: the
+"""The GR00T-style quantized policy (benchmark configs 4 and 5) at reduced depth, against its 'reference' runtime: the
 W2A8 / W8A8 definition with norms and rotary embedding in PyTorch ops (`yanlongvla_b200.definition`), which runs
 nothing of the kernel library.
 

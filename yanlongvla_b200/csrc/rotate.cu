@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, c
                    });
 }
 
-// The rotation op on power-of-two widths D = 2^NL (1024 .. 16384), one row per CTA of D / 32
+// The rotation op on power-of-two widths D = 2^NL (1024 .. 16384: benchmark config 2), one row per CTA of D / 32
 // threads. A thread holds 32 elements at a time: V consecutive ones (index bits 0 .. log2 V - 1) times the 2^WB values
 // of a WB-bit window of index bits [lo, lo + WB), WB = 5 - log2 V (the first window is bits 0..4, i.e. 32 consecutive
 // elements). The butterfly stages of the window's new bits run in registers (low slot a + b, high slot a - b, in the
@@ -632,6 +632,14 @@ int heavy_threads(int M, int N, int CH) {
     return M > tcq_sm_count() && t > 256 ? 256 : t;
 }
 
+// Threads per row of the row kernels of at most 64 registers a thread (post, MLP middles): two 512-thread rows fit on
+// an SM, so up to twice as many rows as SMs take the whole width's threads and still run as one wave; beyond that the
+// launch is throughput-bound and rows get at most 256 threads (more chunks per thread, fewer barriers per element).
+int light_threads(int M, int N, int CH) {
+    const int t = threads_for(N, CH);
+    return M > 2 * tcq_sm_count() && t > 256 ? 256 : t;
+}
+
 // f(std::integral_constant<int, CH>{}) for the chunk width ch (4 or 16).
 template <class F>
 int with_ch(int ch, F f) {
@@ -815,7 +823,7 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
+        const int T = light_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_post<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
             case TCQ_DT_F32: return launch(k_post<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, M, N, lda, col0, st);
@@ -927,7 +935,7 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)6 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
+        const int T = light_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid2<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid2<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
@@ -953,7 +961,7 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     const size_t smem = (size_t)4 * N + (st ? cb : 0);
     return with_ch(rows_ch(M, N, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
-        const int T = threads_for(N, CH);   // 64 registers: two 512-thread rows per SM
+        const int T = light_threads(M, N, CH);
         switch (acc_dtype) {
             case TCQ_DT_I32: return launch(k_mid1<TCQ_DT_I32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);
             case TCQ_DT_F32: return launch(k_mid1<TCQ_DT_F32, CH>, dim3(M), T, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q, (int*)q4, scale, M, N, lda, ldq, st);

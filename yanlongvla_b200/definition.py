@@ -118,7 +118,7 @@ def linear(x, layer, w8, a8=True):
 
 
 def w8a8_linear(x, W, s_ch, bias=None):
-    """W8A8 layer (the vision tower): per-token INT8 activations without rotation, exact product,
+    """W8A8 layer (benchmark config 3, the vision tower): per-token INT8 activations without rotation, exact product,
     y = BF16(((float)acc * s_tok) * s_ch) + bias (a BF16 add)."""
     shape = x.shape
     q, s = quantize_tokens(x.reshape(-1, shape[-1]).float())

@@ -1,4 +1,4 @@
-"""Data-parallel replicas of the quantized policy over the observation batch.
+"""Data-parallel replicas of the quantized policy over the observation batch (benchmark config 5).
 
 The policy shards only over independent observations: rank r of W runs observations [r*B/W, (r+1)*B/W) on its own
 GPU with its own copy of the weights, and the only communication is one gather of the action chunks to rank 0

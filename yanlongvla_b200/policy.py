@@ -1,7 +1,7 @@
-"""A GR00T-style vision-language-action policy with the W2A8 trellis path in every LLM and DiT Linear (BASELINE
+"""A GR00T-style vision-language-action policy with the W2A8 trellis path in every LLM and DiT Linear (benchmark
 config 4) and W8A8 INT8 in the vision tower, random-initialised (no checkpoints travel).
 
-Shape: ViT of 27 layers (hidden 1152, 16 heads, MLP 4304) on 2 camera images of 224 x 224 x 3
+Shape (benchmark config 4): ViT of 27 layers (hidden 1152, 16 heads, MLP 4304) on 2 camera images of 224 x 224 x 3
 uint8 with 14 x 14 patches, pixel-shuffled to 64 tokens each; a 24-layer LLM (hidden 2048, 32 query / 8 KV heads,
 SwiGLU FFN 8192) over 128 image tokens + 32 language tokens (vocab 49152); a 16-block DiT action head (hidden 1536,
 32 heads, FFN 6144) alternating cross-attention to the backbone features (even blocks) and self-attention (odd
@@ -84,7 +84,7 @@ class W8Act:
 
 class W8A8Linear(torch.nn.Module):
     """W8A8 Linear of the vision tower: per-token INT8 activations (no rotation), INT8 weights (N, K) with per-channel
-    FP32 scales, exact INT32 product, y = BF16(((float)acc * s_tok) * s_ch) + bias."""
+    FP32 scales, exact INT32 product, y = BF16(((float)acc * s_tok) * s_ch) + bias (benchmark config 3)."""
     def __init__(self, W, s_ch, bias=None, reference=False):
         super().__init__()
         self.W, self.s_ch, self.bias, self.reference = W, s_ch, bias, reference
