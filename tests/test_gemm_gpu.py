@@ -40,10 +40,10 @@ def test_int_mm_exact(K, M, Kd, N):
     assert np.array_equal(n(acc), ref), f'{int((n(acc) != ref).sum())} mismatches'
 
 
-@pytest.mark.parametrize('M,Kd,N', [(2304, 1024, 2304), (2300, 1040, 2320), (4096, 512, 4608)])
+@pytest.mark.parametrize('M,Kd,N', [(2304, 1024, 2304), (2300, 1040, 2320), (4096, 512, 4608), (1024, 256, 6144), (1000, 272, 6128)])
 def test_int_mm_two_sm_tiles(K, M, Kd, N):
-    """Products large enough for the two-SM 256 x 256 tiles, including M, N and K that are not tile multiples, in all
-    three epilogues (INT32, FP32 and BF16 with the scales)."""
+    """Products large enough for the two-SM 256 x 256 tiles, including M, N and K that are not tile multiples and a
+    partly filled last round of SM pairs, in all three epilogues (INT32, FP32 and BF16 with the scales)."""
     q, w = _rand(M, Kd, N, 1)
     ref = O.int_matmul(q, w)
     assert np.array_equal(n(K.int_mm(t(q), t(w))), ref)
