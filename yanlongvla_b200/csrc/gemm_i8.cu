@@ -637,10 +637,11 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
     __syncthreads();
     tc_fence_after();
     const u32 tmem = *tmem_slot;
-    // The dependency wait is per role: the token tiles (TMA) and everything the epilogue reads or writes in global
-    // memory come after it; the decoders run ahead of it through the first STAGES K stages (the weights and the table
-    // are layer constants), so a launch that starts while its predecessor runs has its first stages decoded by the
-    // time the activations are ready. The MMA issuer touches only shared memory and TMEM.
+    // The dependency wait is per role: the token tiles (TMA), the MMAs that consume them and everything the epilogue
+    // reads or writes in global memory come after it; the decoders run ahead of it through the first STAGES K stages
+    // (the weights and the table are layer constants; those stages' ring slots start free, so nothing waits on a
+    // barrier before the predecessor has finished and every bounded wait keeps its meaning), so a launch that starts
+    // while its predecessor runs has its first stages decoded by the time the activations are ready.
 
     if (warp == 0) {
         pdl_wait();
@@ -656,6 +657,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             }
         }
     } else if (warp == 1) {
+        pdl_wait();
         if (lane == 0) {
             int st = 0;
             u32 ph = 0;
@@ -673,7 +675,6 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             (void)ok;
             mma_commit(tfull);   // also on an early stop: it arrives once every MMA issued so far has finished
         }
-        pdl_wait();
     } else {
         // ---- decoders (tile (di, dj), tile rows 2 dg, 2 dg + 1 of each stage; see load_words)
         const int i = di, j = dj, g = dg;
@@ -681,6 +682,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         int st = 0;
         u32 ph = 0;
         for (int kb = kb0; kb < kb1; ++kb) {
+            if (kb == kb0 + STAGES) pdl_wait();      // beyond the free ring slots: wait for the predecessor first
             const int tc = kb * 8 + j;
             const u32 w0 = pw[0][0], w1 = pw[0][1], w2 = pw[0][2];
             const bool ok = drow_ok && tc < tiles_k;
