@@ -572,11 +572,13 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
               TcParts P, int* __restrict__ ws_acc, int* __restrict__ ws_cnt) {
     constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
     constexpr u32 TMEM_COLS = BN < 32 ? 32 : BN;
-    constexpr u32 IDESC = idesc_i8(BN);
+    // The MMA's N covers the tokens only (M rounded up to 16, a valid UMMA N), not the whole BN-wide token tile: rows
+    // past M of the activation tile are zero-filled and would only cost tensor time (160 tokens in a 256 tile: 3/8).
+    const u32 IDESC = idesc_i8(min(BN, (M + 15) & ~15));
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    u32* tab = reinterpret_cast<u32*>(smem);                         // 128 KB decode table
-    uint8_t* sA = smem + tcq::kTabBytes;
+    char* tab = reinterpret_cast<char*>(smem);                       // 64 KB decode table (16-bit entries)
+    uint8_t* sA = smem + tcq::kTab16Bytes;
     uint8_t* sB = sA + STAGES * A_BYTES;
     u16* pairs = reinterpret_cast<u16*>(sB + STAGES * B_BYTES);       // 1 KB staging of t8 (1024-byte aligned)
     u64* bars = reinterpret_cast<u64*>(sB + STAGES * B_BYTES + 1024);
@@ -632,7 +634,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         if (t1 > t0)
             prefetch_l2_bulk(bits + ((size_t)(tr0 + threadIdx.x) * tiles_k + t0) * 32, (unsigned)(t1 - t0) * 64u);
     }
-    tcq::build_table_i8(tab, pairs, t8 + 1024 * slot);               // weights only: before the dependency wait
+    tcq::build_table16(tab, pairs, t8 + 1024 * slot);                // weights only: before the dependency wait
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -699,7 +701,7 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
             for (int h = 0; h < 2; ++h) {
                 const int row = 16 * i + 2 * g + h;
                 u32 wd[4] = {0, 0, 0, 0};
-                if (ok) tcq::row_words_i8(tcq::rowA(h ? w1 : w0), tcq::rowA(h ? w2 : w1), tab, lane4, wd);
+                if (ok) tcq::row_words16(tcq::rowA(h ? w1 : w0), tcq::rowA(h ? w2 : w1), tab, lane4, wd);
                 *reinterpret_cast<uint4*>(a + row * 128 + ((j ^ (row & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor-core reads
@@ -758,7 +760,9 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
         // barrier keeps every rank's shared memory alive until all have read it. Every thread reaches the barriers.
         // The tile's row scales and the token scales go to shared memory (the A stages, free once the last MMA has
         // completed) before the barrier, so the reduction below reads every operand on chip.
-        float* s_rs = reinterpret_cast<float*>(sA);
+        // (at the end of the operand ring: the accumulator staging, up to 256 x 128 INT32, spans the table and the
+        // first stages)
+        float* s_rs = reinterpret_cast<float*>(sB + STAGES * B_BYTES) - (BM + 256);
         float* s_st = s_rs + BM;
         if (!*abort_flag && warp >= 2) {
             for (int i = threadIdx.x - 64; i < BM + M; i += 32 * kTcDecWarps) {
@@ -782,12 +786,16 @@ k_gemm_tcq_tc(const __grid_constant__ CUtensorMap tmQ, const u16* __restrict__ b
                     const int g = g0 + u * NT;
                     sum[u] = make_int4(0, 0, 0, 0);
                     if (g < g_end) {
+                        if (!P.cl) {
+                            sum[u] = reinterpret_cast<const int4*>(smem)[g];     // no cluster: this CTA's own staging
+                        } else {
 #pragma unroll
-                        for (int r = 0; r < 8; ++r)
-                            if (r < R) {
-                                const int4 a = ld_cluster_v4(peer[r] + 16u * g);
-                                sum[u].x += a.x; sum[u].y += a.y; sum[u].z += a.z; sum[u].w += a.w;
-                            }
+                            for (int r = 0; r < 8; ++r)
+                                if (r < R) {
+                                    const int4 a = ld_cluster_v4(peer[r] + 16u * g);
+                                    sum[u].x += a.x; sum[u].y += a.y; sum[u].z += a.z; sum[u].w += a.w;
+                                }
+                        }
                     }
                 }
 #pragma unroll
@@ -1021,7 +1029,9 @@ int launch_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, const flo
     CUtensorMap tmQ;
     if (!make_map(&tmQ, q, M, K, BN)) return TCQ_ERR_ARG;
     auto kern = k_gemm_tcq_tc<BN, STAGES>;
-    const int smem = 1024 + tcq::kTabBytes + STAGES * (BM + BN) * BK + (2 * STAGES + 1) * 8 + 16 + 1024;
+    const int smem = 1024 + tcq::kTab16Bytes + STAGES * (BM + BN) * BK + (2 * STAGES + 1) * 8 + 16 + 1024;
+    static_assert(tcq::kTab16Bytes + STAGES * (BM + BN) * BK - (BM + 256) * 4 >= 256 * BM * 4 || BN < 256,
+                  "the accumulator staging and the staged scales fit in the table and the ring");
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TCQ_ERR_LAUNCH;
     TcParts P;
     P.ct = (N + BM - 1) / BM;
@@ -1123,10 +1133,10 @@ int tcq_gemm_tcq_tc(const uint16_t* bits, const int8_t* t8, const int8_t* q, con
     if (!workspace || workspace_bytes < tcq_gemm_tcq_tc_workspace(M, N)) return TCQ_ERR_WORKSPACE;
     int* ws = reinterpret_cast<int*>(workspace);
     cudaStream_t st = (cudaStream_t)stream;
-    if (M <= 32) return launch_tc<32, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 64) return launch_tc<64, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    if (M <= 128) return launch_tc<128, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
-    return launch_tc<256, 2>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 32) return launch_tc<32, 6>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 64) return launch_tc<64, 5>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    if (M <= 128) return launch_tc<128, 4>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
+    return launch_tc<256, 3>(bits, t8, q, s, rs, z, M, N, K, nb0, nb1, ws, st);
 }
 
 int tcq_selftest_wait_expiry(unsigned limit_us, void* stream) {

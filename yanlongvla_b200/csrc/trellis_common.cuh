@@ -105,6 +105,48 @@ __device__ __forceinline__ void row_entries(u32 A, u32 B, const u32* tab, u32 la
     e[7] = lut(tab, lane4, off_lo(F3));
 }
 
+// The same table with 16-bit entries (byte 0 = the sign-applied first value, byte 1 = the second), 64 KB: key k of
+// lane l at byte (k >> 1) * 128 + 4 l + 2 (k & 1), so lane l still always reads bank l (a warp's random lookups never
+// conflict) at one more instruction per pair than the 32-bit form. For kernels that need the other 64 KB of shared
+// memory more than that instruction (the tensor-core decode-GEMM's operand ring).
+constexpr int kTab16Bytes = 1024 * 32 * 2;
+
+// Word (row j, any lane) = entry(2j) | entry(2j + 1) << 16; rows 256.. hold the sign keys (first bytes negated).
+__device__ __forceinline__ void build_table16(char* tab, u16* pairs, const i8* __restrict__ t8) {
+    stage_pairs(pairs, t8);
+    const u32* p32 = reinterpret_cast<const u32*>(pairs);
+    uint4* t4 = reinterpret_cast<uint4*>(tab);
+    for (int i = threadIdx.x; i < 512 * 8; i += blockDim.x) {
+        const int j = i >> 3;
+        u32 v = p32[j & 255];
+        if (j >= 256) {
+            const u32 n0 = (0u - v) & 0xffu, n2 = (0u - (v >> 16)) & 0xffu;
+            v = (v & 0xff00ff00u) | n0 | (n2 << 16);
+        }
+        t4[i] = make_uint4(v, v, v, v);
+    }
+}
+
+// Lookup of x = (s + 1) s in the 16-bit table: (x & 0xFF80) | 4 l | ((x >> 5) & 2).
+__device__ __forceinline__ u32 lut16(const char* tab, u32 lane4, u32 x) {
+    return *reinterpret_cast<const u16*>(tab + ((x & 0xFF80u) | lane4 | ((x >> 5) & 2u)));
+}
+
+// INT8 weights of one tile row as 4 words from the 16-bit table (A, B as in row_entries: the upper half of F_p is
+// state p, its lower half state p + 4; junk above bit 16 of a state never reaches bits 6..15 of (s + 1) s).
+__device__ __forceinline__ void row_words16(u32 A, u32 B, const char* tab, u32 lane4, u32 (&w)[4]) {
+    const u32 Fs[4] = {A, __funnelshift_l(B, A, 4), __funnelshift_l(B, A, 8), __funnelshift_l(B, A, 12)};
+    u32 e[8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const u32 v = __umulhi(Fs[p], 65536u);
+        e[p] = lut16(tab, lane4, v * v + v);
+        e[p + 4] = lut16(tab, lane4, Fs[p] * Fs[p] + Fs[p]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = __byte_perm(e[2 * j], e[2 * j + 1], 0x5410);
+}
+
 // INT8 weights of one tile row as 4 little-endian words (columns 4j .. 4j+3 in word j).
 __device__ __forceinline__ void row_words_i8(u32 A, u32 B, const u32* tab, u32 lane4, u32 (&w)[4]) {
     u32 e[8];
