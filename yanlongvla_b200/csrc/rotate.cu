@@ -176,38 +176,19 @@ struct Win2 {
 template <int NL>
 constexpr int rot_vec() { return NL >= 12 ? 2 : 4; }
 
-template <int DT, int OT, int NL>
-__global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
-                                                            void* __restrict__ y, int inverse) {
-    constexpr int D = 1 << NL, V = rot_vec<NL>();
+// The windowed block Walsh of one power-of-two row of D = 2^NL elements held by D / 32 threads, 32 each: on entry v is
+// the thread's window 0 (its 32 consecutive elements 32 t .. 32 t + 31); on return v is the unscaled transform in the
+// last window's layout (register V q + k holds element win_elem<NL>(t, q, k)). buf: D + D / 2^WB floats of shared
+// memory for the exchanges. REUSE: buf may still be read by another thread's previous use, so the first exchange
+// waits for the whole block first. Contains __syncthreads().
+template <int NL, bool REUSE>
+__device__ __forceinline__ void win_walsh(float (&v)[32], float* buf, int t) {
+    constexpr int V = rot_vec<NL>();
     using W = Win2<NL, V>;
     constexpr int VB = W::VB, WB = W::WB, G = 1 << WB;
     static_assert(NL >= 2 * WB + VB, "every window after the first needs lo - log2 V >= WB");
     using VecT = typename std::conditional<V == 2, float2, float4>::type;
-    extern __shared__ __align__(16) float buf[];
     VecT* bv = reinterpret_cast<VecT*>(buf);
-    i8* ssg = reinterpret_cast<i8*>(buf + D + (D >> WB));          // inverse: the row's signs, for the last window
-    pdl_launch_dependents();
-    const int t = threadIdx.x;
-    if (inverse) {                                                  // 32 signs per thread (read after a barrier below)
-        const uint4* src = reinterpret_cast<const uint4*>(sg) + 2 * t;
-        uint4* dst = reinterpret_cast<uint4*>(ssg) + 2 * t;
-        dst[0] = __ldg(src);
-        dst[1] = __ldg(src + 1);
-    }
-    pdl_wait();
-    const size_t row = blockIdx.x;
-    float v[32];
-    {
-        const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
-        loadc<DT, 32>(reinterpret_cast<const char*>(x) + (row * D + 32 * t) * es, v);
-        if (!inverse) {
-            float s32[32];
-            load_signsc<32, true>(sg + 32 * t, s32);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] = v[k] * s32[k];
-        }
-    }
     // element of register r in window p: (r % V) | thread bits at VB .. lo - 1 | (r / V) << lo | thread bits >= lo + WB
     auto ebase = [&](int lo) { return ((t & ((1 << (lo - VB)) - 1)) << VB) | ((t >> (lo - VB)) << (lo + WB)); };
 #pragma unroll
@@ -241,7 +222,7 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
                 }
         }
         if (p + 1 < W::P) {
-            if (p > 0) __syncthreads();                    // every thread has read window p before it is overwritten
+            if (p > 0 || REUSE) __syncthreads();           // every thread has read buf before it is overwritten
 #pragma unroll
             for (int q = 0; q < G; ++q) {
                 if constexpr (V == 2) bv[ph0 + q * gstep] = make_float2(v[2 * q], v[2 * q + 1]);
@@ -250,13 +231,80 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __rest
             __syncthreads();
         }
     }
+}
+
+// Element of register V q + k of thread t after win_walsh (the last window's layout).
+template <int NL>
+__device__ __forceinline__ int win_elem(int t, int q, int k) {
+    constexpr int V = rot_vec<NL>();
+    using W = Win2<NL, V>;
+    constexpr int VB = W::VB, WB = W::WB, LO = W::lo(W::P - 1);
+    return (((t & ((1 << (LO - VB)) - 1)) << VB) | ((t >> (LO - VB)) << (LO + WB))) + (q << LO) + k;
+}
+
+// Back to window 0 through buf: v in the last window's layout -> the thread's 32 consecutive elements (buf as in
+// win_walsh; waits for the block before writing and after).
+template <int NL>
+__device__ __forceinline__ void win_relayout(float (&v)[32], float* buf, int t) {
+    constexpr int V = rot_vec<NL>();
+    constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
+    using VecT = typename std::conditional<V == 2, float2, float4>::type;
+    VecT* bv = reinterpret_cast<VecT*>(buf);
+    auto ph = [](int g) { return g + (g >> WB); };
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+        const int g = win_elem<NL>(t, q, 0) / V;
+        if constexpr (V == 2) bv[ph(g)] = make_float2(v[2 * q], v[2 * q + 1]);
+        else bv[ph(g)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    __syncthreads();
+    const int p0 = ph(t << WB);                                      // window 0: 2^WB consecutive groups, one period
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+        const VecT a = bv[p0 + q];
+        if constexpr (V == 2) {
+            v[2 * q] = a.x; v[2 * q + 1] = a.y;
+        } else {
+            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+        }
+    }
+}
+
+template <int DT, int OT, int NL>
+__global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
+                                                            void* __restrict__ y, int inverse) {
+    constexpr int D = 1 << NL, V = rot_vec<NL>();
+    constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
+    extern __shared__ __align__(16) float buf[];
+    i8* ssg = reinterpret_cast<i8*>(buf + D + (D >> WB));          // inverse: the row's signs, for the last window
+    pdl_launch_dependents();
+    const int t = threadIdx.x;
+    if (inverse) {                                                  // 32 signs per thread (read after a barrier below)
+        const uint4* src = reinterpret_cast<const uint4*>(sg) + 2 * t;
+        uint4* dst = reinterpret_cast<uint4*>(ssg) + 2 * t;
+        dst[0] = __ldg(src);
+        dst[1] = __ldg(src + 1);
+    }
+    pdl_wait();
+    const size_t row = blockIdx.x;
+    float v[32];
+    {
+        const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+        loadc<DT, 32>(reinterpret_cast<const char*>(x) + (row * D + 32 * t) * es, v);
+        if (!inverse) {
+            float s32[32];
+            load_signsc<32, true>(sg + 32 * t, s32);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = v[k] * s32[k];
+        }
+    }
+    win_walsh<NL, false>(v, buf, t);
     // the last window: scale, signs (inverse), V consecutive outputs per store
-    constexpr int LO = W::lo(W::P - 1);
-    const int e0 = ebase(LO);
     const float sc = wscale(D);
 #pragma unroll
     for (int q = 0; q < G; ++q) {
-        const int e = e0 + (q << LO);
+        const int e = win_elem<NL>(t, q, 0);
         float o[V];
 #pragma unroll
         for (int k = 0; k < V; ++k) o[k] = v[V * q + k] * sc;
@@ -536,6 +584,81 @@ __global__ void __launch_bounds__(512, 2) k_mid2(const void* __restrict__ acc, c
     row_walshc<CH>(buf, N, [&](int c, float* v) { buf_chunk<CH>(buf, c, v); },
                    [&](int i0, const float* v) { store_chunk<CH>(buf, i0, v, mx); },
                    [&](int i, float v) { buf[swz(i)] = v; mx = fmaxf(mx, fabsf(v)); });
+    quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
+// The gated-MLP middle on a power-of-two width N = 2^NL (1024 .. 16384: the LLM's 8192): the same arithmetic as
+// k_mid2, each of its three block Walsh transforms done by win_walsh (32 elements per thread, register windows,
+// two or three shared-memory exchanges) instead of the general row transform. The gate and up transforms end in the
+// same register layout, so g * u is formed in registers; one exchange brings the product back to window 0 for the
+// third transform; the finished row goes through shared memory to quantize_store (the common quantizer).
+template <int AT, int NL>
+__global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restrict__ acc, const float* __restrict__ s,
+                                                          const float* __restrict__ rs, const i8* __restrict__ sv,
+                                                          const u16* __restrict__ lut, const i8* __restrict__ su,
+                                                          int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale,
+                                                          int lda, int ldq) {
+    constexpr int N = 1 << NL, V = rot_vec<NL>();
+    constexpr int G = 1 << Win2<NL, V>::WB;
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    const int t = threadIdx.x;
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * lda;
+    const float st = s ? s[tok] : 1.f;
+    const float sc = wscale(N);
+    float v[32];
+    auto load_half = [&](int off) {                 // window 0 of z = SCALE(acc[base + off + i])
+        const float* r = rs ? rs + off + 32 * t : nullptr;
+        load_scaledc<AT, 16>(acc, base + off + 32 * t, st, r, v);
+        load_scaledc<AT, 16>(acc, base + off + 32 * t + 16, st, r ? r + 16 : nullptr, v + 16);
+    };
+    // gate: g = lut(BF16(post(gate))), kept as BF16 pairs in registers
+    load_half(0);
+    win_walsh<NL, false>(v, buf, t);
+    u32 gw[16];
+#pragma unroll
+    for (int qq = 0; qq < G; ++qq) {
+        const int e = win_elem<NL>(t, qq, 0);
+#pragma unroll
+        for (int k = 0; k < V; k += 2) {
+            const int r = V * qq + k;
+            const u16 g0 = __ldg(lut + f2bf((v[r] * sc) * (float)sv[e + k]));
+            const u16 g1 = __ldg(lut + f2bf((v[r + 1] * sc) * (float)sv[e + k + 1]));
+            gw[r >> 1] = (u32)g0 | ((u32)g1 << 16);
+        }
+    }
+    // up, then x = BF16(g * u) * su in registers
+    load_half(N);
+    win_walsh<NL, true>(v, buf, t);
+#pragma unroll
+    for (int qq = 0; qq < G; ++qq) {
+        const int e = win_elem<NL>(t, qq, 0);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const int r = V * qq + k;
+            const u16 u = f2bf((v[r] * sc) * (float)sv[N + e + k]);
+            const u16 g = (u16)(gw[r >> 1] >> (16 * (r & 1)));
+            v[r] = bf2f(f2bf(bf2f(g) * bf2f(u))) * (float)su[e + k];
+        }
+    }
+    // the next layer's pre: block Walsh of x, INT8 (quantize_store reads the finished row at swz positions)
+    win_relayout<NL>(v, buf, t);
+    win_walsh<NL, true>(v, buf, t);
+    __syncthreads();                                // every thread has read buf in the last window
+    float mx = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < G; ++qq) {
+        const int e = win_elem<NL>(t, qq, 0);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const float o = v[V * qq + k] * sc;
+            buf[swz(e + k)] = o;
+            mx = fmaxf(mx, fabsf(o));
+        }
+    }
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
@@ -929,6 +1052,27 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!acc_aligned(acc, acc_dtype, lda, N) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
+    // Power-of-two widths in a latency-bound launch (at most two rows per SM): the register-window transforms
+    // (k_mid2_p2), one row of N / 32 threads per block. Many-row launches keep k_mid2, whose 64 registers a thread let
+    // twice as many rows share an SM.
+    if ((N & (N - 1)) == 0 && N >= 1024 && N <= 16384 && (acc_dtype == TCQ_DT_I32 || acc_dtype == TCQ_DT_F32) &&
+        M <= 2 * tcq_sm_count()) {
+        auto go = [&](auto nl) {
+            constexpr int NL = decltype(nl)::value;
+            constexpr int WB = Win2<NL, rot_vec<NL>()>::WB;
+            const size_t smem = (size_t)4 * ((1 << NL) + ((1 << NL) >> WB));
+            auto kern = acc_dtype == TCQ_DT_I32 ? k_mid2_p2<TCQ_DT_I32, NL> : k_mid2_p2<TCQ_DT_F32, NL>;
+            return launch(kern, dim3(M), (1 << NL) / 32, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q,
+                          (int*)q4, scale, lda, ldq);
+        };
+        switch (N) {
+            case 1024: return go(std::integral_constant<int, 10>{});
+            case 2048: return go(std::integral_constant<int, 11>{});
+            case 4096: return go(std::integral_constant<int, 12>{});
+            case 8192: return go(std::integral_constant<int, 13>{});
+            default: return go(std::integral_constant<int, 14>{});
+        }
+    }
     // Staged layer constants (as k_mid2 stages them): rs of both layers (I32 / BF16 accumulators), sv of both, su.
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 8 * N : 0) + 2 * N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
