@@ -599,11 +599,16 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
                                                           int8_t* __restrict__ q, int* __restrict__ q4, float* __restrict__ scale,
                                                           int lda, int ldq) {
     constexpr int N = 1 << NL, V = rot_vec<NL>();
-    constexpr int G = 1 << Win2<NL, V>::WB;
+    constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
     extern __shared__ __align__(16) float buf[];
     __shared__ float red[32];
+    // sv of both layers and su staged in shared memory before the dependency wait (layer constants)
+    i8* ssv = reinterpret_cast<i8*>(buf + N + (N >> WB));
+    i8* ssu = ssv + 2 * N;
     pdl_launch_dependents();
     const int t = threadIdx.x;
+    for (int i = t; i < 2 * N / 16; i += N / 32) reinterpret_cast<uint4*>(ssv)[i] = __ldg(reinterpret_cast<const uint4*>(sv) + i);
+    for (int i = t; i < N / 16; i += N / 32) reinterpret_cast<uint4*>(ssu)[i] = __ldg(reinterpret_cast<const uint4*>(su) + i);
     pdl_wait();
     const int tok = blockIdx.x;
     const size_t base = (size_t)tok * lda;
@@ -615,8 +620,12 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
         load_scaledc<AT, 16>(acc, base + off + 32 * t, st, r, v);
         load_scaledc<AT, 16>(acc, base + off + 32 * t + 16, st, r ? r + 16 : nullptr, v + 16);
     };
-    // gate: g = lut(BF16(post(gate))), kept as BF16 pairs in registers
+    // gate: g = lut(BF16(post(gate))), kept as BF16 pairs in registers; the up half's 128 bytes per thread (and its
+    // row scales) are requested into L1 now, to be read after the gate transform
     load_half(0);
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const char*>(acc) + (base + N + 32 * t) * 4));
+    if (rs) asm volatile("prefetch.global.L1 [%0];" ::"l"(rs + N + 32 * t));
+    __syncthreads();                                // the staged constants are complete
     win_walsh<NL, false>(v, buf, t);
     u32 gw[16];
 #pragma unroll
@@ -625,8 +634,8 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
 #pragma unroll
         for (int k = 0; k < V; k += 2) {
             const int r = V * qq + k;
-            const u16 g0 = __ldg(lut + f2bf((v[r] * sc) * (float)sv[e + k]));
-            const u16 g1 = __ldg(lut + f2bf((v[r + 1] * sc) * (float)sv[e + k + 1]));
+            const u16 g0 = __ldg(lut + f2bf((v[r] * sc) * (float)ssv[e + k]));
+            const u16 g1 = __ldg(lut + f2bf((v[r + 1] * sc) * (float)ssv[e + k + 1]));
             gw[r >> 1] = (u32)g0 | ((u32)g1 << 16);
         }
     }
@@ -639,9 +648,9 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
 #pragma unroll
         for (int k = 0; k < V; ++k) {
             const int r = V * qq + k;
-            const u16 u = f2bf((v[r] * sc) * (float)sv[N + e + k]);
+            const u16 u = f2bf((v[r] * sc) * (float)ssv[N + e + k]);
             const u16 g = (u16)(gw[r >> 1] >> (16 * (r & 1)));
-            v[r] = bf2f(f2bf(bf2f(g) * bf2f(u))) * (float)su[e + k];
+            v[r] = bf2f(f2bf(bf2f(g) * bf2f(u))) * (float)ssu[e + k];
         }
     }
     // the next layer's pre: block Walsh of x, INT8 (quantize_store reads the finished row at swz positions)
@@ -1052,15 +1061,15 @@ int tcq_mid2(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!acc_aligned(acc, acc_dtype, lda, N) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
-    // Power-of-two widths in a latency-bound launch (at most two rows per SM): the register-window transforms
+    // Power-of-two widths in a latency-bound launch (at most two rows per SM; sv 16-byte aligned): the register-window transforms
     // (k_mid2_p2), one row of N / 32 threads per block. Many-row launches keep k_mid2, whose 64 registers a thread let
     // twice as many rows share an SM.
     if ((N & (N - 1)) == 0 && N >= 1024 && N <= 16384 && (acc_dtype == TCQ_DT_I32 || acc_dtype == TCQ_DT_F32) &&
-        M <= 2 * tcq_sm_count()) {
+        M <= 2 * tcq_sm_count() && tcq_aligned(sv, 16)) {
         auto go = [&](auto nl) {
             constexpr int NL = decltype(nl)::value;
             constexpr int WB = Win2<NL, rot_vec<NL>()>::WB;
-            const size_t smem = (size_t)4 * ((1 << NL) + ((1 << NL) >> WB));
+            const size_t smem = (size_t)4 * ((1 << NL) + ((1 << NL) >> WB)) + 3 * (1 << NL);   // + staged sv, su
             auto kern = acc_dtype == TCQ_DT_I32 ? k_mid2_p2<TCQ_DT_I32, NL> : k_mid2_p2<TCQ_DT_F32, NL>;
             return launch(kern, dim3(M), (1 << NL) / 32, smem, stream, acc, s, rs, (const i8*)sv, (const u16*)lut, (const i8*)su, q,
                           (int*)q4, scale, lda, ldq);
