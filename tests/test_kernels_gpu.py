@@ -266,7 +266,8 @@ def _mlp_inputs(M, N, seed):
 
 
 @pytest.mark.parametrize('act', ['gelu', 'silu'])
-@pytest.mark.parametrize('M,N', [(10, 4096), (3, 4304), (17, 1536), (2, 16384), (5, 8192), (2, 12288), (160, 8192)])
+@pytest.mark.parametrize('M,N', [(10, 4096), (3, 4304), (17, 1536), (2, 16384), (5, 8192), (2, 12288), (160, 8192), (17, 6144),
+                                 (1, 3072), (400, 2048)])
 def test_mlp_middles(K, act, M, N):
     acc, s, rs, sv, su, bias = _mlp_inputs(M, N, 0)
     lut = n(K.act_table(act))

@@ -181,7 +181,15 @@ constexpr int rot_vec() { return NL >= 12 ? 2 : 4; }
 // last window's layout (register V q + k holds element win_elem<NL>(t, q, k)). buf: D + D / 2^WB floats of shared
 // memory for the exchanges. REUSE: buf may still be read by another thread's previous use, so the first exchange
 // waits for the whole block first. Contains __syncthreads().
-template <int NL, bool REUSE>
+// Block barrier: the usual aligned one, or the unaligned form for code where the threads of a block take different
+// branches that each execute the same number of barriers (two power-of-two blocks of one row, below).
+template <bool ALIGNED>
+__device__ __forceinline__ void blk_sync() {
+    if constexpr (ALIGNED) __syncthreads();
+    else asm volatile("barrier.sync 0;" ::: "memory");
+}
+
+template <int NL, bool REUSE, bool ALIGNED = true>
 __device__ __forceinline__ void win_walsh(float (&v)[32], float* buf, int t) {
     constexpr int V = rot_vec<NL>();
     using W = Win2<NL, V>;
@@ -222,13 +230,13 @@ __device__ __forceinline__ void win_walsh(float (&v)[32], float* buf, int t) {
                 }
         }
         if (p + 1 < W::P) {
-            if (p > 0 || REUSE) __syncthreads();           // every thread has read buf before it is overwritten
+            if (p > 0 || REUSE) blk_sync<ALIGNED>();       // every thread has read buf before it is overwritten
 #pragma unroll
             for (int q = 0; q < G; ++q) {
                 if constexpr (V == 2) bv[ph0 + q * gstep] = make_float2(v[2 * q], v[2 * q + 1]);
                 else bv[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
-            __syncthreads();
+            blk_sync<ALIGNED>();
         }
     }
 }
@@ -244,21 +252,21 @@ __device__ __forceinline__ int win_elem(int t, int q, int k) {
 
 // Back to window 0 through buf: v in the last window's layout -> the thread's 32 consecutive elements (buf as in
 // win_walsh; waits for the block before writing and after).
-template <int NL>
+template <int NL, bool ALIGNED = true>
 __device__ __forceinline__ void win_relayout(float (&v)[32], float* buf, int t) {
     constexpr int V = rot_vec<NL>();
     constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
     using VecT = typename std::conditional<V == 2, float2, float4>::type;
     VecT* bv = reinterpret_cast<VecT*>(buf);
     auto ph = [](int g) { return g + (g >> WB); };
-    __syncthreads();
+    blk_sync<ALIGNED>();
 #pragma unroll
     for (int q = 0; q < G; ++q) {
         const int g = win_elem<NL>(t, q, 0) / V;
         if constexpr (V == 2) bv[ph(g)] = make_float2(v[2 * q], v[2 * q + 1]);
         else bv[ph(g)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
-    __syncthreads();
+    blk_sync<ALIGNED>();
     const int p0 = ph(t << WB);                                      // window 0: 2^WB consecutive groups, one period
 #pragma unroll
     for (int q = 0; q < G; ++q) {
@@ -668,6 +676,79 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
             mx = fmaxf(mx, fabsf(o));
         }
     }
+    quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
+}
+
+// The plain-MLP middle on widths of one or two power-of-two blocks, N = 2^NL0 (+ 2^NL1), whose windowed transforms
+// take the same number of windows (6144 = 4096 + 2048, the DiT's; 1536, 3072, 12288; powers of two 1024 .. 16384):
+// the arithmetic of k_mid1, each block's two transforms done by win_walsh on its own 2^NL / 32 threads. The two
+// blocks' threads run different code that executes the same barriers the same number of times, so the barriers
+// there are the unaligned form. Layer constants (sv, su, bias) are staged before the dependency wait.
+template <int AT, int NL0, int NL1>
+__global__ void __launch_bounds__(((1 << NL0) + (NL1 ? (1 << NL1) : 0)) / 32)
+k_mid1_2b(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs, const i8* __restrict__ sv,
+          const float* __restrict__ bias, const u16* __restrict__ lut, const i8* __restrict__ su, int8_t* __restrict__ q,
+          int* __restrict__ q4, float* __restrict__ scale, int lda, int ldq) {
+    constexpr int NLB = NL1 ? NL1 : NL0;                          // (the second block's parameters when there is one)
+    constexpr int N0 = 1 << NL0, N1 = NL1 ? 1 << NL1 : 0, N = N0 + N1, T0 = N0 / 32;
+    constexpr int WB0 = Win2<NL0, rot_vec<NL0>()>::WB, WB1 = Win2<NLB, rot_vec<NLB>()>::WB;
+    static_assert(!NL1 || (NL1 < NL0 && Win2<NL0, rot_vec<NL0>()>::P == Win2<NLB, rot_vec<NLB>()>::P),
+                  "the two blocks' transforms execute the same barriers");
+    extern __shared__ __align__(16) float buf[];
+    float* buf0 = buf;
+    float* buf1 = buf + N0 + (N0 >> WB0);
+    float* sbias = buf1 + (NL1 ? N1 + (N1 >> WB1) : 0);
+    i8* ssv = reinterpret_cast<i8*>(sbias + (bias ? N : 0));
+    i8* ssu = ssv + N;
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    const int t = threadIdx.x, nt = N / 32;
+    for (int i = t; i < N / 16; i += nt) {
+        reinterpret_cast<uint4*>(ssv)[i] = __ldg(reinterpret_cast<const uint4*>(sv) + i);
+        reinterpret_cast<uint4*>(ssu)[i] = __ldg(reinterpret_cast<const uint4*>(su) + i);
+    }
+    if (bias)
+        for (int i = t; i < N / 4; i += nt) reinterpret_cast<float4*>(sbias)[i] = __ldg(reinterpret_cast<const float4*>(bias) + i);
+    __syncthreads();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * lda;
+    const float st = s ? s[tok] : 1.f;
+    float mx = 0.f;
+    auto run_block = [&](auto nlc, int tb, int off, float* bb) {
+        constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
+        const float sc = wscale(1 << NL);
+        float v[32];
+        const float* r = rs ? rs + off + 32 * tb : nullptr;
+        load_scaledc<AT, 16>(acc, base + off + 32 * tb, st, r, v);
+        load_scaledc<AT, 16>(acc, base + off + 32 * tb + 16, st, r ? r + 16 : nullptr, v + 16);
+        win_walsh<NL, false, false>(v, bb, tb);
+#pragma unroll
+        for (int qq = 0; qq < G; ++qq) {
+            const int e = off + win_elem<NL>(tb, qq, 0);
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                float y = (v[V * qq + k] * sc) * (float)ssv[e + k];
+                if (bias) y = y + sbias[e + k];
+                v[V * qq + k] = bf2f(__ldg(lut + f2bf(y))) * (float)ssu[e + k];
+            }
+        }
+        win_relayout<NL, false>(v, bb, tb);
+        win_walsh<NL, true, false>(v, bb, tb);
+        blk_sync<false>();                          // both blocks' last reads are done: buf is rewritten below
+#pragma unroll
+        for (int qq = 0; qq < G; ++qq) {
+            const int e = off + win_elem<NL>(tb, qq, 0);
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                const float o = v[V * qq + k] * sc;
+                buf[swz(e + k)] = o;
+                mx = fmaxf(mx, fabsf(o));
+            }
+        }
+    };
+    if (t < T0) run_block(std::integral_constant<int, NL0>{}, t, 0, buf0);
+    else if constexpr (NL1 != 0) run_block(std::integral_constant<int, NLB>{}, t - T0, N0, buf1);
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
@@ -1108,6 +1189,34 @@ int tcq_mid1(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!acc_aligned(acc, acc_dtype, lda, 0) || (rs && !tcq_aligned(rs, 16)) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16)))
         return TCQ_ERR_ALIGN;
+    // Widths of one or two power-of-two blocks with equal window counts, in a latency-bound launch (at most two rows
+    // per SM): the register-window transforms (k_mid1_2b).
+    if ((acc_dtype == TCQ_DT_I32 || acc_dtype == TCQ_DT_F32) && M <= 2 * tcq_sm_count() && tcq_aligned(sv, 16) &&
+        (!bias || tcq_aligned(bias, 16))) {
+        auto go = [&](auto n0, auto n1) {
+            constexpr int NL0 = decltype(n0)::value, NL1 = decltype(n1)::value, NLB = NL1 ? NL1 : NL0;
+            constexpr int NN = (1 << NL0) + (NL1 ? 1 << NL1 : 0);
+            const size_t smem = (size_t)4 * ((1 << NL0) + ((1 << NL0) >> Win2<NL0, rot_vec<NL0>()>::WB)) +
+                                (NL1 ? (size_t)4 * ((1 << NLB) + ((1 << NLB) >> Win2<NLB, rot_vec<NLB>()>::WB)) : 0) +
+                                (bias ? (size_t)4 * NN : 0) + 2 * (size_t)NN;
+            auto kern = acc_dtype == TCQ_DT_I32 ? k_mid1_2b<TCQ_DT_I32, NL0, NL1> : k_mid1_2b<TCQ_DT_F32, NL0, NL1>;
+            return launch(kern, dim3(M), NN / 32, smem, stream, acc, s, rs, (const i8*)sv, bias, (const u16*)lut, (const i8*)su, q,
+                          (int*)q4, scale, lda, ldq);
+        };
+        using std::integral_constant;
+        switch (N) {
+            case 1536: return go(integral_constant<int, 10>{}, integral_constant<int, 9>{});
+            case 3072: return go(integral_constant<int, 11>{}, integral_constant<int, 10>{});
+            case 6144: return go(integral_constant<int, 12>{}, integral_constant<int, 11>{});
+            case 12288: return go(integral_constant<int, 13>{}, integral_constant<int, 12>{});
+            case 1024: return go(integral_constant<int, 10>{}, integral_constant<int, 0>{});
+            case 2048: return go(integral_constant<int, 11>{}, integral_constant<int, 0>{});
+            case 4096: return go(integral_constant<int, 12>{}, integral_constant<int, 0>{});
+            case 8192: return go(integral_constant<int, 13>{}, integral_constant<int, 0>{});
+            case 16384: return go(integral_constant<int, 14>{}, integral_constant<int, 0>{});
+            default: break;
+        }
+    }
     // Staged layer constants (as k_mid1 stages them): rs (I32 / BF16 accumulators), bias, sv, su.
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
