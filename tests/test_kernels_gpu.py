@@ -209,7 +209,7 @@ def test_bf16_rounding_special_values(K):
 
 
 @pytest.mark.parametrize('dt', ['bf16', 'f16', 'f32'])
-@pytest.mark.parametrize('Kd', [16, 48, 1152, 4304, 12288, 16384])
+@pytest.mark.parametrize('Kd', [16, 48, 1152, 1536, 2048, 4304, 6144, 12288, 16384])
 def test_pre_dtypes_and_widths(K, dt, Kd):
     M = 6
     x = cases.activations(f'pre{Kd}', M, Kd, dt)
@@ -229,7 +229,7 @@ def test_pre_dtypes_and_widths(K, dt, Kd):
 
 
 @pytest.mark.parametrize('acc_dt', ['i32', 'f32', 'bf16'])
-@pytest.mark.parametrize('N', [16, 80, 1536, 4304, 16384])
+@pytest.mark.parametrize('N', [16, 80, 1536, 2048, 4304, 6144, 16384])
 def test_post_acc_types(K, acc_dt, N):
     M = 3
     r = cases.rng('post', N, acc_dt)

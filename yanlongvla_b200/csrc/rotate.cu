@@ -679,6 +679,133 @@ __global__ void __launch_bounds__((1 << NL) / 32) k_mid2_p2(const void* __restri
     quantize_store(buf, mx, red, q, q4, scale, tok, N, ldq);
 }
 
+// One row transform on a width of one or two power-of-two blocks (as k_mid1_2b): load(e0, v) fills the 32 inputs
+// e0 .. e0 + 31 of a thread's window 0, fin(e, v, sc, V) takes V finished unscaled outputs e .. e + V - 1 and the
+// block's scale. A block-wide barrier separates the transform's last shared-memory reads from fin, which may rewrite
+// buf. buf: the exchange areas of both blocks (as k_mid1_2b). Every thread of the row's block calls this.
+template <int NL0, int NL1, class Load, class Fin>
+__device__ __forceinline__ void row2b_transform(float* buf, int t, Load load, Fin fin) {
+    constexpr int NLB = NL1 ? NL1 : NL0, N0 = 1 << NL0, T0 = N0 / 32;
+    constexpr int WB0 = Win2<NL0, rot_vec<NL0>()>::WB;
+    static_assert(!NL1 || (NL1 < NL0 && Win2<NL0, rot_vec<NL0>()>::P == Win2<NLB, rot_vec<NLB>()>::P),
+                  "the two blocks' transforms execute the same barriers");
+    auto run = [&](auto nlc, int tb, int off, float* bb) {
+        constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
+        float v[32];
+        load(off + 32 * tb, v);
+        win_walsh<NL, true, false>(v, bb, tb);
+        blk_sync<false>();
+        const float sc = wscale(1 << NL);
+#pragma unroll
+        for (int qq = 0; qq < G; ++qq) fin(off + win_elem<NL>(tb, qq, 0), v + V * qq, sc, std::integral_constant<int, V>{});
+    };
+    if (t < T0) run(std::integral_constant<int, NL0>{}, t, 0, buf);
+    else if constexpr (NL1 != 0) run(std::integral_constant<int, NLB>{}, t - T0, N0, buf + N0 + (N0 >> WB0));
+}
+
+// Shared memory of row2b_transform's exchange areas, in floats.
+template <int NL0, int NL1>
+constexpr int row2b_floats() {
+    constexpr int NLB = NL1 ? NL1 : NL0;
+    return (1 << NL0) + ((1 << NL0) >> Win2<NL0, rot_vec<NL0>()>::WB) +
+           (NL1 ? (1 << NLB) + ((1 << NLB) >> Win2<NLB, rot_vec<NLB>()>::WB) : 0);
+}
+
+// pre (k_pre's arithmetic) on widths of one or two power-of-two blocks, for latency-bound launches.
+template <int DT, int NL0, int NL1>
+__global__ void __launch_bounds__(((1 << NL0) + (NL1 ? (1 << NL1) : 0)) / 32)
+k_pre_2b(const void* __restrict__ x, const i8* __restrict__ su, int8_t* __restrict__ q, int* __restrict__ q4,
+         float* __restrict__ scale, int ldq) {
+    constexpr int K = (1 << NL0) + (NL1 ? (1 << NL1) : 0);
+    extern __shared__ __align__(16) float buf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t es = DT == TCQ_DT_F32 ? 4 : 2;
+    const char* xr = reinterpret_cast<const char*>(x) + (size_t)tok * K * es;
+    float mx = 0.f;
+    row2b_transform<NL0, NL1>(buf, threadIdx.x,
+        [&](int e0, float* v) {
+            float sg[32];
+            loadc<DT, 32>(xr + (size_t)e0 * es, v);
+            load_signsc<32, true>(su + e0, sg);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = v[k] * sg[k];
+        },
+        [&](int e, const float* v, float sc, auto vc) {
+#pragma unroll
+            for (int k = 0; k < decltype(vc)::value; ++k) {
+                const float o = v[k] * sc;
+                buf[swz(e + k)] = o;
+                mx = fmaxf(mx, fabsf(o));
+            }
+        });
+    quantize_store(buf, mx, red, q, q4, scale, tok, K, ldq);
+}
+
+// post (k_post's arithmetic) on widths of one or two power-of-two blocks, for latency-bound launches; sv and bias
+// staged before the dependency wait.
+template <int AT, int NL0, int NL1>
+__global__ void __launch_bounds__(((1 << NL0) + (NL1 ? (1 << NL1) : 0)) / 32)
+k_post_2b(const void* __restrict__ acc, const float* __restrict__ s, const float* __restrict__ rs, const i8* __restrict__ sv,
+          const float* __restrict__ bias, u16* __restrict__ y, int lda, int col0) {
+    constexpr int N = (1 << NL0) + (NL1 ? (1 << NL1) : 0);
+    extern __shared__ __align__(16) float buf[];
+    float* sbias = buf + row2b_floats<NL0, NL1>();
+    i8* ssv = reinterpret_cast<i8*>(sbias + (bias ? N : 0));
+    pdl_launch_dependents();
+    const int t = threadIdx.x, nt = N / 32;
+    for (int i = t; i < N / 16; i += nt) reinterpret_cast<uint4*>(ssv)[i] = __ldg(reinterpret_cast<const uint4*>(sv) + i);
+    if (bias)
+        for (int i = t; i < N / 4; i += nt) reinterpret_cast<float4*>(sbias)[i] = __ldg(reinterpret_cast<const float4*>(bias) + i);
+    __syncthreads();
+    pdl_wait();
+    const int tok = blockIdx.x;
+    const size_t base = (size_t)tok * lda + col0;
+    const float st = s ? s[tok] : 1.f;
+    u16* yo = y + (size_t)tok * N;
+    row2b_transform<NL0, NL1>(buf, t,
+        [&](int e0, float* v) {
+            const float* r = rs ? rs + e0 : nullptr;
+            load_scaledc<AT, 16>(acc, base + e0, st, r, v);
+            load_scaledc<AT, 16>(acc, base + e0 + 16, st, r ? r + 16 : nullptr, v + 16);
+        },
+        [&](int e, const float* v, float sc, auto vc) {
+            constexpr int V = decltype(vc)::value;
+            u16 o[V];
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                float z = (v[k] * sc) * (float)ssv[e + k];
+                if (bias) z = z + sbias[e + k];
+                o[k] = f2bf(z);
+            }
+            if constexpr (V == 2) {
+                *reinterpret_cast<u32*>(yo + e) = (u32)o[0] | ((u32)o[1] << 16);
+            } else {
+                *reinterpret_cast<uint2*>(yo + e) = make_uint2((u32)o[0] | ((u32)o[1] << 16), (u32)o[2] | ((u32)o[3] << 16));
+            }
+        });
+}
+
+// f(integral_constant NL0, integral_constant NL1) for the widths the two-block kernels take; -1 otherwise.
+template <class F>
+int with_2b(int N, F f) {
+    using std::integral_constant;
+    switch (N) {
+        case 1536: return f(integral_constant<int, 10>{}, integral_constant<int, 9>{});
+        case 3072: return f(integral_constant<int, 11>{}, integral_constant<int, 10>{});
+        case 6144: return f(integral_constant<int, 12>{}, integral_constant<int, 11>{});
+        case 12288: return f(integral_constant<int, 13>{}, integral_constant<int, 12>{});
+        case 1024: return f(integral_constant<int, 10>{}, integral_constant<int, 0>{});
+        case 2048: return f(integral_constant<int, 11>{}, integral_constant<int, 0>{});
+        case 4096: return f(integral_constant<int, 12>{}, integral_constant<int, 0>{});
+        case 8192: return f(integral_constant<int, 13>{}, integral_constant<int, 0>{});
+        case 16384: return f(integral_constant<int, 14>{}, integral_constant<int, 0>{});
+        default: return -1;
+    }
+}
+
 // The plain-MLP middle on widths of one or two power-of-two blocks, N = 2^NL0 (+ 2^NL1), whose windowed transforms
 // take the same number of windows (6144 = 4096 + 2048, the DiT's; 1536, 3072, 12288; powers of two 1024 .. 16384):
 // the arithmetic of k_mid1, each block's two transforms done by win_walsh on its own 2^NL / 32 threads. The two
@@ -943,6 +1070,18 @@ int tcq_pre(const void* x, int x_dtype, const int8_t* su, int8_t* q, int32_t* q4
     if (M <= 0 || !width_ok(K)) return TCQ_ERR_SHAPE;
     if (q4 && ldq < M) return TCQ_ERR_ARG;
     if (!tcq_aligned(x, 16) || !tcq_aligned(su, 16) || (q && !tcq_aligned(q, 16))) return TCQ_ERR_ALIGN;
+    // Widths of one or two power-of-two blocks in a latency-bound launch: the register-window transform (k_pre_2b).
+    if (M <= 2 * tcq_sm_count() && (x_dtype == TCQ_DT_BF16 || x_dtype == TCQ_DT_F16 || x_dtype == TCQ_DT_F32)) {
+        const int e = with_2b(K, [&](auto n0, auto n1) {
+            constexpr int NL0 = decltype(n0)::value, NL1 = decltype(n1)::value;
+            constexpr int T = ((1 << NL0) + (NL1 ? (1 << NL1) : 0)) / 32;
+            const size_t sm = (size_t)4 * row2b_floats<NL0, NL1>();
+            auto kern = x_dtype == TCQ_DT_BF16 ? k_pre_2b<TCQ_DT_BF16, NL0, NL1>
+                        : x_dtype == TCQ_DT_F16 ? k_pre_2b<TCQ_DT_F16, NL0, NL1> : k_pre_2b<TCQ_DT_F32, NL0, NL1>;
+            return launch(kern, dim3(M), T, sm, stream, x, (const i8*)su, q, (int*)q4, scale, ldq);
+        });
+        if (e >= 0) return e;
+    }
     const size_t smem = (size_t)4 * K;
     return with_ch(rows_ch(M, K, kLightPerSm), [&](auto C) {
         constexpr int CH = decltype(C)::value;
@@ -1030,6 +1169,18 @@ int tcq_post(const void* acc, int acc_dtype, const float* s, const float* rs, co
     if (acc_dtype == TCQ_DT_BF16 && !rs) return TCQ_ERR_ARG;
     if (M <= 0 || !width_ok(N) || col0 < 0 || lda < col0 + N) return TCQ_ERR_SHAPE;
     if (!acc_aligned(acc, acc_dtype, lda, col0) || (rs && !tcq_aligned(rs, 16))) return TCQ_ERR_ALIGN;
+    // Widths of one or two power-of-two blocks in a latency-bound launch: the register-window transform (k_post_2b).
+    if (M <= 2 * tcq_sm_count() && (acc_dtype == TCQ_DT_I32 || acc_dtype == TCQ_DT_F32) && tcq_aligned(sv, 16) &&
+        (!bias || tcq_aligned(bias, 16)) && tcq_aligned(y, 16)) {
+        const int e = with_2b(N, [&](auto n0, auto n1) {
+            constexpr int NL0 = decltype(n0)::value, NL1 = decltype(n1)::value;
+            constexpr int NN = (1 << NL0) + (NL1 ? (1 << NL1) : 0);
+            const size_t sm = (size_t)4 * row2b_floats<NL0, NL1>() + (bias ? (size_t)4 * NN : 0) + NN;
+            auto kern = acc_dtype == TCQ_DT_I32 ? k_post_2b<TCQ_DT_I32, NL0, NL1> : k_post_2b<TCQ_DT_F32, NL0, NL1>;
+            return launch(kern, dim3(M), NN / 32, sm, stream, acc, s, rs, (const i8*)sv, bias, (u16*)y, lda, col0);
+        });
+        if (e >= 0) return e;
+    }
     // Staged layer constants (as k_post stages them): rs (I32 / BF16 accumulators), bias, sv.
     const size_t cb = (size_t)(acc_dtype != TCQ_DT_F32 && rs ? 4 * N : 0) + (bias ? 4 * N : 0) + N;
     const int st = tcq_stage_rows(M, cb, kStageMaxBytes);
