@@ -164,121 +164,6 @@ __global__ void __launch_bounds__(512, 1) k_rotate(const void* __restrict__ x, c
 // V = 2 (WB = 4) takes two exchanges at D = 4096 and 8192 where V = 4 (WB = 3) takes three (16 instead of 24 bytes
 // of shared-memory traffic per element: 4096 x 4096 in 20.0 instead of 23.0 us), and at 16384 three either way but
 // wins 2 % there; at 1024 and 2048 the counts are equal and V = 4 moves them with half the instructions.
-template <int NL, int V>
-struct Win2 {
-    static_assert(V == 2 || V == 4, "exchange vectors of 2 or 4 floats");
-    static constexpr int VB = V == 2 ? 1 : 2, WB = 5 - VB;
-    static constexpr int P = 1 + (NL - 5 + WB - 1) / WB;                                 // windows
-    static constexpr int first(int p) { return p == 0 ? 0 : 5 + WB * (p - 1); }        // first index bit new in window p
-    static constexpr int lo(int p) { return p == 0 ? VB : (first(p) + WB <= NL ? first(p) : NL - WB); }
-};
-
-template <int NL>
-constexpr int rot_vec() { return NL >= 12 ? 2 : 4; }
-
-// The windowed block Walsh of one power-of-two row of D = 2^NL elements held by D / 32 threads, 32 each: on entry v is
-// the thread's window 0 (its 32 consecutive elements 32 t .. 32 t + 31); on return v is the unscaled transform in the
-// last window's layout (register V q + k holds element win_elem<NL>(t, q, k)). buf: D + D / 2^WB floats of shared
-// memory for the exchanges. REUSE: buf may still be read by another thread's previous use, so the first exchange
-// waits for the whole block first. Contains __syncthreads().
-// Block barrier: the usual aligned one, or the unaligned form for code where the threads of a block take different
-// branches that each execute the same number of barriers (two power-of-two blocks of one row, below).
-template <bool ALIGNED>
-__device__ __forceinline__ void blk_sync() {
-    if constexpr (ALIGNED) __syncthreads();
-    else asm volatile("barrier.sync 0;" ::: "memory");
-}
-
-template <int NL, bool REUSE, bool ALIGNED = true>
-__device__ __forceinline__ void win_walsh(float (&v)[32], float* buf, int t) {
-    constexpr int V = rot_vec<NL>();
-    using W = Win2<NL, V>;
-    constexpr int VB = W::VB, WB = W::WB, G = 1 << WB;
-    static_assert(NL >= 2 * WB + VB, "every window after the first needs lo - log2 V >= WB");
-    using VecT = typename std::conditional<V == 2, float2, float4>::type;
-    VecT* bv = reinterpret_cast<VecT*>(buf);
-    // element of register r in window p: (r % V) | thread bits at VB .. lo - 1 | (r / V) << lo | thread bits >= lo + WB
-    auto ebase = [&](int lo) { return ((t & ((1 << (lo - VB)) - 1)) << VB) | ((t >> (lo - VB)) << (lo + WB)); };
-#pragma unroll
-    for (int p = 0; p < W::P; ++p) {
-        const int lo = W::lo(p);
-        const int g0 = ebase(lo) >> VB, ph0 = g0 + (g0 >> WB);       // padded group of register group 0
-        // padded step between register groups (window 0: consecutive groups within one padding period)
-        const int gstep = p == 0 ? 1 : (1 << (lo - VB)) + (1 << (lo - VB - WB));
-        if (p > 0) {
-#pragma unroll
-            for (int q = 0; q < G; ++q) {
-                const VecT a = bv[ph0 + q * gstep];
-                if constexpr (V == 2) {
-                    v[2 * q] = a.x; v[2 * q + 1] = a.y;
-                } else {
-                    v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-                }
-            }
-        }
-#pragma unroll
-        for (int sb = 0; sb < 5; ++sb) {
-            const int bit = sb < VB ? sb : lo + sb - VB;
-            if (bit < W::first(p) || (p > 0 && sb < VB)) continue;
-            const int hh = 1 << sb;
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-                if (!(k & hh)) {
-                    const float a = v[k], b = v[k + hh];
-                    v[k] = a + b;
-                    v[k + hh] = a - b;
-                }
-        }
-        if (p + 1 < W::P) {
-            if (p > 0 || REUSE) blk_sync<ALIGNED>();       // every thread has read buf before it is overwritten
-#pragma unroll
-            for (int q = 0; q < G; ++q) {
-                if constexpr (V == 2) bv[ph0 + q * gstep] = make_float2(v[2 * q], v[2 * q + 1]);
-                else bv[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            }
-            blk_sync<ALIGNED>();
-        }
-    }
-}
-
-// Element of register V q + k of thread t after win_walsh (the last window's layout).
-template <int NL>
-__device__ __forceinline__ int win_elem(int t, int q, int k) {
-    constexpr int V = rot_vec<NL>();
-    using W = Win2<NL, V>;
-    constexpr int VB = W::VB, WB = W::WB, LO = W::lo(W::P - 1);
-    return (((t & ((1 << (LO - VB)) - 1)) << VB) | ((t >> (LO - VB)) << (LO + WB))) + (q << LO) + k;
-}
-
-// Back to window 0 through buf: v in the last window's layout -> the thread's 32 consecutive elements (buf as in
-// win_walsh; waits for the block before writing and after).
-template <int NL, bool ALIGNED = true>
-__device__ __forceinline__ void win_relayout(float (&v)[32], float* buf, int t) {
-    constexpr int V = rot_vec<NL>();
-    constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
-    using VecT = typename std::conditional<V == 2, float2, float4>::type;
-    VecT* bv = reinterpret_cast<VecT*>(buf);
-    auto ph = [](int g) { return g + (g >> WB); };
-    blk_sync<ALIGNED>();
-#pragma unroll
-    for (int q = 0; q < G; ++q) {
-        const int g = win_elem<NL>(t, q, 0) / V;
-        if constexpr (V == 2) bv[ph(g)] = make_float2(v[2 * q], v[2 * q + 1]);
-        else bv[ph(g)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    }
-    blk_sync<ALIGNED>();
-    const int p0 = ph(t << WB);                                      // window 0: 2^WB consecutive groups, one period
-#pragma unroll
-    for (int q = 0; q < G; ++q) {
-        const VecT a = bv[p0 + q];
-        if constexpr (V == 2) {
-            v[2 * q] = a.x; v[2 * q + 1] = a.y;
-        } else {
-            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
-        }
-    }
-}
-
 template <int DT, int OT, int NL>
 __global__ void __launch_bounds__((1 << NL) / 32) k_rotate_p2(const void* __restrict__ x, const i8* __restrict__ sg,
                                                             void* __restrict__ y, int inverse) {
@@ -693,8 +578,8 @@ __device__ __forceinline__ void row2b_transform(float* buf, int t, Load load, Fi
         constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
         float v[32];
         load(off + 32 * tb, v);
-        win_walsh<NL, true, false>(v, bb, tb);
-        blk_sync<false>();
+        win_walsh<NL, true, 1>(v, bb, tb);
+        blk_sync<1>();
         const float sc = wscale(1 << NL);
 #pragma unroll
         for (int qq = 0; qq < G; ++qq) fin(off + win_elem<NL>(tb, qq, 0), v + V * qq, sc, std::integral_constant<int, V>{});
@@ -849,7 +734,7 @@ k_mid1_2b(const void* __restrict__ acc, const float* __restrict__ s, const float
         const float* r = rs ? rs + off + 32 * tb : nullptr;
         load_scaledc<AT, 16>(acc, base + off + 32 * tb, st, r, v);
         load_scaledc<AT, 16>(acc, base + off + 32 * tb + 16, st, r ? r + 16 : nullptr, v + 16);
-        win_walsh<NL, false, false>(v, bb, tb);
+        win_walsh<NL, false, 1>(v, bb, tb);
 #pragma unroll
         for (int qq = 0; qq < G; ++qq) {
             const int e = off + win_elem<NL>(tb, qq, 0);
@@ -860,9 +745,9 @@ k_mid1_2b(const void* __restrict__ acc, const float* __restrict__ s, const float
                 v[V * qq + k] = bf2f(__ldg(lut + f2bf(y))) * (float)ssu[e + k];
             }
         }
-        win_relayout<NL, false>(v, bb, tb);
-        win_walsh<NL, true, false>(v, bb, tb);
-        blk_sync<false>();                          // both blocks' last reads are done: buf is rewritten below
+        win_relayout<NL, 1>(v, bb, tb);
+        win_walsh<NL, true, 1>(v, bb, tb);
+        blk_sync<1>();                          // both blocks' last reads are done: buf is rewritten below
 #pragma unroll
         for (int qq = 0; qq < G; ++qq) {
             const int e = off + win_elem<NL>(tb, qq, 0);

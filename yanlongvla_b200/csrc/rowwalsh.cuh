@@ -11,6 +11,8 @@
 // launch of a few rows (bound by the latency of each thread's instruction stream) finishes sooner. The arithmetic is
 // the same for both: only which thread performs an addition changes, never its operands or their order.
 #pragma once
+#include <type_traits>
+
 #include "tcq_common.cuh"
 
 namespace tcq {
@@ -333,5 +335,130 @@ __device__ __forceinline__ void load_scaledc(const void* acc, size_t idx, float 
         for (int k = 0; k < CH; ++k) v[k] = v[k] * r[k];
     }
 }
+
+// ---------------------------------------------------------------------------------------------------- windowed transform
+// The block Walsh of one power-of-two row of D = 2^NL elements (1024 .. 16384) held by D / 32 threads, 32 elements
+// each, in register windows: a thread's 32 elements are V consecutive ones (V = 2 from 4096 wide, 4 below) times the
+// 2^(5 - log2 V) values of a window of index bits; the window's new butterfly stages run in registers in the
+// definition's order (h = 1, 2, 4, ...), so the sums are the row transform's bit for bit; between windows the row
+// passes through shared memory as groups of V floats with one padding group per 2^(5 - log2 V) (conflict-free).
+template <int NL, int V>
+struct Win2 {
+    static_assert(V == 2 || V == 4, "exchange vectors of 2 or 4 floats");
+    static constexpr int VB = V == 2 ? 1 : 2, WB = 5 - VB;
+    static constexpr int P = 1 + (NL - 5 + WB - 1) / WB;                                 // windows
+    static constexpr int first(int p) { return p == 0 ? 0 : 5 + WB * (p - 1); }        // first index bit new in window p
+    static constexpr int lo(int p) { return p == 0 ? VB : (first(p) + WB <= NL ? first(p) : NL - WB); }
+};
+
+template <int NL>
+constexpr int rot_vec() { return NL >= 12 ? 2 : 4; }
+
+// The windowed block Walsh of one power-of-two row of D = 2^NL elements held by D / 32 threads, 32 each: on entry v is
+// the thread's window 0 (its 32 consecutive elements 32 t .. 32 t + 31); on return v is the unscaled transform in the
+// last window's layout (register V q + k holds element win_elem<NL>(t, q, k)). buf: D + D / 2^WB floats of shared
+// memory for the exchanges. REUSE: buf may still be read by another thread's previous use, so the first exchange
+// waits for the whole block first. Contains __syncthreads().
+// Barrier of the threads that run a windowed transform. BAR 0: the whole block (__syncthreads); 1: the whole block in
+// the unaligned form, for code where the threads take different branches that each execute the same number of
+// barriers (two power-of-two blocks of one row); 2: only the first NT threads (named barrier 1), for a transform run
+// by part of a larger block.
+template <int BAR, int NT = 0>
+__device__ __forceinline__ void blk_sync() {
+    if constexpr (BAR == 0) __syncthreads();
+    else if constexpr (BAR == 1) asm volatile("barrier.sync 0;" ::: "memory");
+    else asm volatile("barrier.sync 1, %0;" ::"n"(NT) : "memory");
+}
+
+template <int NL, bool REUSE, int BAR = 0>
+__device__ __forceinline__ void win_walsh(float (&v)[32], float* buf, int t) {
+    constexpr int V = rot_vec<NL>();
+    using W = Win2<NL, V>;
+    constexpr int VB = W::VB, WB = W::WB, G = 1 << WB;
+    static_assert(NL >= 2 * WB + VB, "every window after the first needs lo - log2 V >= WB");
+    using VecT = typename std::conditional<V == 2, float2, float4>::type;
+    VecT* bv = reinterpret_cast<VecT*>(buf);
+    // element of register r in window p: (r % V) | thread bits at VB .. lo - 1 | (r / V) << lo | thread bits >= lo + WB
+    auto ebase = [&](int lo) { return ((t & ((1 << (lo - VB)) - 1)) << VB) | ((t >> (lo - VB)) << (lo + WB)); };
+#pragma unroll
+    for (int p = 0; p < W::P; ++p) {
+        const int lo = W::lo(p);
+        const int g0 = ebase(lo) >> VB, ph0 = g0 + (g0 >> WB);       // padded group of register group 0
+        // padded step between register groups (window 0: consecutive groups within one padding period)
+        const int gstep = p == 0 ? 1 : (1 << (lo - VB)) + (1 << (lo - VB - WB));
+        if (p > 0) {
+#pragma unroll
+            for (int q = 0; q < G; ++q) {
+                const VecT a = bv[ph0 + q * gstep];
+                if constexpr (V == 2) {
+                    v[2 * q] = a.x; v[2 * q + 1] = a.y;
+                } else {
+                    v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int sb = 0; sb < 5; ++sb) {
+            const int bit = sb < VB ? sb : lo + sb - VB;
+            if (bit < W::first(p) || (p > 0 && sb < VB)) continue;
+            const int hh = 1 << sb;
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+                if (!(k & hh)) {
+                    const float a = v[k], b = v[k + hh];
+                    v[k] = a + b;
+                    v[k + hh] = a - b;
+                }
+        }
+        if (p + 1 < W::P) {
+            if (p > 0 || REUSE) blk_sync<BAR, (1 << NL) / 32>();       // every thread has read buf before it is overwritten
+#pragma unroll
+            for (int q = 0; q < G; ++q) {
+                if constexpr (V == 2) bv[ph0 + q * gstep] = make_float2(v[2 * q], v[2 * q + 1]);
+                else bv[ph0 + q * gstep] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+            blk_sync<BAR, (1 << NL) / 32>();
+        }
+    }
+}
+
+// Element of register V q + k of thread t after win_walsh (the last window's layout).
+template <int NL>
+__device__ __forceinline__ int win_elem(int t, int q, int k) {
+    constexpr int V = rot_vec<NL>();
+    using W = Win2<NL, V>;
+    constexpr int VB = W::VB, WB = W::WB, LO = W::lo(W::P - 1);
+    return (((t & ((1 << (LO - VB)) - 1)) << VB) | ((t >> (LO - VB)) << (LO + WB))) + (q << LO) + k;
+}
+
+// Back to window 0 through buf: v in the last window's layout -> the thread's 32 consecutive elements (buf as in
+// win_walsh; waits for the block before writing and after).
+template <int NL, int BAR = 0>
+__device__ __forceinline__ void win_relayout(float (&v)[32], float* buf, int t) {
+    constexpr int V = rot_vec<NL>();
+    constexpr int WB = Win2<NL, V>::WB, G = 1 << WB;
+    using VecT = typename std::conditional<V == 2, float2, float4>::type;
+    VecT* bv = reinterpret_cast<VecT*>(buf);
+    auto ph = [](int g) { return g + (g >> WB); };
+    blk_sync<BAR, (1 << NL) / 32>();
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+        const int g = win_elem<NL>(t, q, 0) / V;
+        if constexpr (V == 2) bv[ph(g)] = make_float2(v[2 * q], v[2 * q + 1]);
+        else bv[ph(g)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    blk_sync<BAR, (1 << NL) / 32>();
+    const int p0 = ph(t << WB);                                      // window 0: 2^WB consecutive groups, one period
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+        const VecT a = bv[p0 + q];
+        if constexpr (V == 2) {
+            v[2 * q] = a.x; v[2 * q + 1] = a.y;
+        } else {
+            v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+        }
+    }
+}
+
 
 }  // namespace tcq

@@ -252,12 +252,52 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     const float sv = !FX && (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
     // FX: the pre of the M rows into shared memory (Walsh buffer, then q4 words (K/4, M) and ss).
     float* sbuf = reinterpret_cast<float*>(reinterpret_cast<char*>(tab + kTabBytes / 4) + (CO ? (kThreads / 32) * kUnitBytes : 0));
-    int* sq4 = reinterpret_cast<int*>(sbuf + K);
+    int* sq4 = reinterpret_cast<int*>(sbuf + K + K / 8);   // (the windowed transform's exchange area: K + K / 8 floats)
     if constexpr (FX) {
         const size_t es = xdt == TCQ_DT_F32 ? 4 : 2;
+        const int nl = (K & (K - 1)) == 0 && K >= 1024 && K <= 8192 ? 31 - __clz(K) : 0;
         for (int m = 0; m < M; ++m) {
             const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
             float mx = 0.f;
+            if (nl) {
+                // Power-of-two widths: the register-window transform on the first K / 32 threads (a named barrier
+                // among them); the rest wait at the quantizer's block barrier.
+                auto pre_win = [&](auto nlc) {
+                    constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
+                    const int t = threadIdx.x;
+                    if (t < (1 << NL) / 32) {
+                        float v[32], sg[32];
+                        if (xdt == TCQ_DT_BF16) loadc<TCQ_DT_BF16, 32>(xr + (size_t)32 * t * es, v);
+                        else if (xdt == TCQ_DT_F16) loadc<TCQ_DT_F16, 32>(xr + (size_t)32 * t * es, v);
+                        else loadc<TCQ_DT_F32, 32>(xr + (size_t)32 * t * es, v);
+                        load_signsc<32, true>(su + 32 * t, sg);
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) v[k] = v[k] * sg[k];
+                        win_walsh<NL, true, 2>(v, sbuf, t);
+                        blk_sync<2, (1 << NL) / 32>();          // the transform's last reads of sbuf are done
+                        const float sc = wscale(1 << NL);
+#pragma unroll
+                        for (int qq = 0; qq < G; ++qq) {
+                            const int e = win_elem<NL>(t, qq, 0);
+#pragma unroll
+                            for (int k = 0; k < V; ++k) {
+                                const float o = v[V * qq + k] * sc;
+                                sbuf[swz(e + k)] = o;
+                                mx = fmaxf(mx, fabsf(o));
+                            }
+                        }
+                    }
+                };
+                switch (nl) {
+                    case 10: pre_win(std::integral_constant<int, 10>{}); break;
+                    case 11: pre_win(std::integral_constant<int, 11>{}); break;
+                    case 12: pre_win(std::integral_constant<int, 12>{}); break;
+                    default: pre_win(std::integral_constant<int, 13>{}); break;
+                }
+                quantize_store(sbuf, mx, red, nullptr, sq4, ss, m, K, M);
+                __syncthreads();                   // sbuf is rewritten by the next row; sq4 / ss complete
+                continue;
+            }
             // Chunks of 4: a few rows on 512 threads, where per-thread latency bounds the transform.
             row_walshc<4>(sbuf, K,
                           [&](int cc, float* v) {
@@ -554,7 +594,7 @@ int launch_gemm_tcq(const uint16_t* bits, const int8_t* t8, const int32_t* q4, c
     p.pf_lead = nl == 1 && max_units <= 2 * (kThreads / 32) ? std::max(1, (cta * 5) / 16) : 0;
     const bool fx = xin != nullptr;
     auto kern = fx ? k_gemm_tcq<MT, LT, (MT <= 4)> : k_gemm_tcq<MT, LT, false>;
-    const int smem = kTabBytes + (LT == 1 ? (kThreads / 32) * kUnitBytes : 0) + (fx ? K * 4 + K * MT : 0);
+    const int smem = kTabBytes + (LT == 1 ? (kThreads / 32) * kUnitBytes : 0) + (fx ? K * 4 + K / 2 + K * MT : 0);
     if (fx && (MT > 4 || smem > kFxMaxSmem)) return TCQ_ERR_SHAPE;
     if (set_smem(kern, smem)) return TCQ_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
