@@ -132,7 +132,8 @@ def test_gemm_tcq_one_token_unaligned_activations(K):
 
 @pytest.mark.parametrize('M,N,Kd,dt', [(1, 4096, 4096, 'bf16'), (1, 512, 1152, 'f16'), (2, 2048, 8192, 'f32'),
                                        (3, 1536, 1536, 'bf16'), (4, 6144, 1152, 'bf16'), (1, 8192, 8192, 'bf16'),
-                                       (4, 48, 80, 'f32')])
+                                       (4, 48, 80, 'f32'), (1, 2048, 1024, 'f16'), (1, 1536, 2048, 'f32'),
+                                       (1, 4112, 4096, 'bf16'), (2, 4096, 4096, 'f16')])
 def test_gemm_tcq_x_fused_pre(K, M, N, Kd, dt):
     """pre fused into the decode-GEMV (tcq_gemm_tcq_x): z equals the oracle's pre + product bit for bit."""
     L = DevLayer(f'gx{N}x{Kd}', N, Kd, False)

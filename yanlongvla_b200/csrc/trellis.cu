@@ -199,10 +199,16 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     const int row_first = (int)fdiv(ub, parts.fS);
     const int nrows = ub < ue ? (int)fdiv(ue - 1, parts.fS) - row_first + 1 : 0;
 
+    // FX with one token and a power-of-two K (1024 .. 8192): the first K / 32 threads (the pre threads) start the pre's
+    // transform at once, waiting only for the previous kernel, while the other threads request the table and fill it;
+    // the two halves meet at the quantizer. Otherwise every thread builds the table, then waits, then runs the pre.
+    const int nl = FX && (K & (K - 1)) == 0 && K >= 1024 && K <= 8192 ? 31 - __clz(K) : 0;
+    const int PT = nl && M == 1 ? K / 32 : 0;
+    const int tq = (int)threadIdx.x - PT;          // index among the threads that build the table
     // The 1 KB table is the CTA's first memory request: the table build waits for it, and under a full HBM stream
     // a request queued behind this CTA's weight loads returns about a microsecond later.
     uint4 t8v = make_uint4(0, 0, 0, 0);
-    if (threadIdx.x < 64) t8v = ldg_table_v4(reinterpret_cast<const uint4*>(t8 + 1024 * slot) + threadIdx.x);
+    if (tq >= 0 && tq < 64) t8v = ldg_table_v4(reinterpret_cast<const uint4*>(t8 + 1024 * slot) + tq);
     // The CTAs of a launch start one by one, in index order, as the previous launch's CTAs leave their SMs (over
     // about one launch time). When each CTA has little work, CTA c asks L2 for the stream of CTA c + pf_lead, which
     // starts about a DRAM latency later and then finds its weights in L2 instead of waiting on DRAM.
@@ -232,6 +238,23 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         for (int j = 0; j < 4; ++j)
             L[j] = sg * TPU + 8 * j + (lane >> 2) < tiles ? ldg_stream_v4(base + 32 * j + lane) : make_uint4(0, 0, 0, 0);
     };
+    // CO: a unit's 2 KB (Ln, as loaded) -> this lane's tile words W through the warp's staging area.
+    auto stage_unit = [&](const uint4 (&L)[4], u32 (&W)[RPT + 1]) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = 8 * j + (lane >> 2), c = lane & 3;
+            *reinterpret_cast<uint4*>(stage + 64 * t + 16 * (c ^ ((t >> 1) & 3))) = L[j];
+        }
+        __syncwarp();
+        const char* mine = stage + 64 * lane;
+        const int x = (lane >> 1) & 3;
+        const uint4 c0 = *reinterpret_cast<const uint4*>(mine + 16 * (0 ^ x)), c1 = *reinterpret_cast<const uint4*>(mine + 16 * (1 ^ x)),
+                    c2 = *reinterpret_cast<const uint4*>(mine + 16 * (2 ^ x)), c3 = *reinterpret_cast<const uint4*>(mine + 16 * (3 ^ x));
+        __syncwarp();
+        const u32 all[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+#pragma unroll
+        for (int a = 0; a <= RPT; ++a) W[a] = all[a & 15];
+    };
     u32 Wn[RPT + 1];
     uint4 Ln[4];
     if (u < ue) {
@@ -244,56 +267,75 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
     // behind it: the row scales (layer constants) before the dependency wait, the token scales right after it.
     const int nrs = nrows * 16;                    // <= kMaxRows * 16 <= kThreads
     const float rsv = (int)threadIdx.x < nrs ? __ldg(rs + (size_t)(tb + row_first) * 16 + threadIdx.x) : 0.f;
-    if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = t8v;
-    __syncthreads();
-    fill_table_i8_nt<kThreads>(tab, pairs);
-    __syncthreads();
-    pdl_wait();                                    // activations / scales come from the previous kernel
-    const float sv = !FX && (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
     // FX: the pre of the M rows into shared memory (Walsh buffer, then q4 words (K/4, M) and ss).
     float* sbuf = reinterpret_cast<float*>(reinterpret_cast<char*>(tab + kTabBytes / 4) + (CO ? (kThreads / 32) * kUnitBytes : 0));
     int* sq4 = reinterpret_cast<int*>(sbuf + K + K / 8);   // (the windowed transform's exchange area: K + K / 8 floats)
-    if constexpr (FX) {
-        const size_t es = xdt == TCQ_DT_F32 ? 4 : 2;
-        const int nl = (K & (K - 1)) == 0 && K >= 1024 && K <= 8192 ? 31 - __clz(K) : 0;
-        for (int m = 0; m < M; ++m) {
-            const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
-            float mx = 0.f;
-            if (nl) {
-                // Power-of-two widths: the register-window transform on the first K / 32 threads (a named barrier
-                // among them); the rest wait at the quantizer's block barrier.
-                auto pre_win = [&](auto nlc) {
-                    constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
-                    const int t = threadIdx.x;
-                    if (t < (1 << NL) / 32) {
-                        float v[32], sg[32];
-                        if (xdt == TCQ_DT_BF16) loadc<TCQ_DT_BF16, 32>(xr + (size_t)32 * t * es, v);
-                        else if (xdt == TCQ_DT_F16) loadc<TCQ_DT_F16, 32>(xr + (size_t)32 * t * es, v);
-                        else loadc<TCQ_DT_F32, 32>(xr + (size_t)32 * t * es, v);
-                        load_signsc<32, true>(su + 32 * t, sg);
+    const size_t es = xdt == TCQ_DT_F32 ? 4 : 2;
+    float mx = 0.f;
+    // Power-of-two widths: the register-window transform of token row m on the first K / 32 threads (a named barrier
+    // among them): the scaled result into sbuf, its absolute maximum into mx.
+    auto pre_win_row = [&](int m) {
+        const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
+        auto pre_win = [&](auto nlc) {
+            constexpr int NL = decltype(nlc)::value, V = rot_vec<NL>(), G = 1 << Win2<NL, V>::WB;
+            const int t = threadIdx.x;
+            if (t < (1 << NL) / 32) {
+                float v[32], sg[32];
+                if (xdt == TCQ_DT_BF16) loadc<TCQ_DT_BF16, 32>(xr + (size_t)32 * t * es, v);
+                else if (xdt == TCQ_DT_F16) loadc<TCQ_DT_F16, 32>(xr + (size_t)32 * t * es, v);
+                else loadc<TCQ_DT_F32, 32>(xr + (size_t)32 * t * es, v);
+                load_signsc<32, true>(su + 32 * t, sg);
 #pragma unroll
-                        for (int k = 0; k < 32; ++k) v[k] = v[k] * sg[k];
-                        win_walsh<NL, true, 2>(v, sbuf, t);
-                        blk_sync<2, (1 << NL) / 32>();          // the transform's last reads of sbuf are done
-                        const float sc = wscale(1 << NL);
+                for (int k = 0; k < 32; ++k) v[k] = v[k] * sg[k];
+                win_walsh<NL, true, 2>(v, sbuf, t);
+                blk_sync<2, (1 << NL) / 32>();          // the transform's last reads of sbuf are done
+                const float sc = wscale(1 << NL);
 #pragma unroll
-                        for (int qq = 0; qq < G; ++qq) {
-                            const int e = win_elem<NL>(t, qq, 0);
+                for (int qq = 0; qq < G; ++qq) {
+                    const int e = win_elem<NL>(t, qq, 0);
 #pragma unroll
-                            for (int k = 0; k < V; ++k) {
-                                const float o = v[V * qq + k] * sc;
-                                sbuf[swz(e + k)] = o;
-                                mx = fmaxf(mx, fabsf(o));
-                            }
-                        }
+                    for (int k = 0; k < V; ++k) {
+                        const float o = v[V * qq + k] * sc;
+                        sbuf[swz(e + k)] = o;
+                        mx = fmaxf(mx, fabsf(o));
                     }
-                };
-                switch (nl) {
-                    case 10: pre_win(std::integral_constant<int, 10>{}); break;
-                    case 11: pre_win(std::integral_constant<int, 11>{}); break;
-                    case 12: pre_win(std::integral_constant<int, 12>{}); break;
-                    default: pre_win(std::integral_constant<int, 13>{}); break;
                 }
+            }
+        };
+        switch (nl) {
+            case 10: pre_win(std::integral_constant<int, 10>{}); break;
+            case 11: pre_win(std::integral_constant<int, 11>{}); break;
+            case 12: pre_win(std::integral_constant<int, 12>{}); break;
+            default: pre_win(std::integral_constant<int, 13>{}); break;
+        }
+    };
+    if (PT == 0) {
+        if (threadIdx.x < 64) reinterpret_cast<uint4*>(pairs)[threadIdx.x] = t8v;
+        __syncthreads();
+        fill_table_i8_nt<kThreads>(tab, pairs);
+    } else if ((int)threadIdx.x < PT) {
+        if constexpr (FX) {
+            pdl_wait();                            // the activations come from the previous kernel
+            pre_win_row(0);
+        }
+    } else {
+        if (tq < 64) reinterpret_cast<uint4*>(pairs)[tq] = t8v;
+        asm volatile("barrier.sync 2, %0;" ::"r"(kThreads - PT) : "memory");
+        fill_table_i8_span(tab, pairs, tq, kThreads - PT);
+    }
+    __syncthreads();
+    pdl_wait();                                    // activations / scales come from the previous kernel
+    const float sv = !FX && (int)threadIdx.x < M && threadIdx.x < MT ? s[threadIdx.x] : 0.f;
+    if constexpr (FX) {
+        if (PT) {
+            quantize_store(sbuf, mx, red, nullptr, sq4, ss, 0, K, M);
+            __syncthreads();                       // sq4 / ss complete
+        }
+        for (int m = 0; m < M && !PT; ++m) {
+            const char* xr = reinterpret_cast<const char*>(xin) + (size_t)m * K * es;
+            mx = 0.f;
+            if (nl) {
+                pre_win_row(m);                    // the other threads wait at the quantizer's block barrier
                 quantize_store(sbuf, mx, red, nullptr, sq4, ss, m, K, M);
                 __syncthreads();                   // sbuf is rewritten by the next row; sq4 / ss complete
                 continue;
@@ -322,20 +364,7 @@ k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* _
         int rn = rrel, sn = seg + nw;              // the warp's next unit
         while (sn >= S) { sn -= S; ++rn; }
         if constexpr (CO) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int t = 8 * j + (lane >> 2), c = lane & 3;
-                *reinterpret_cast<uint4*>(stage + 64 * t + 16 * (c ^ ((t >> 1) & 3))) = Ln[j];
-            }
-            __syncwarp();
-            const char* mine = stage + 64 * lane;
-            const int x = (lane >> 1) & 3;
-            const uint4 c0 = *reinterpret_cast<const uint4*>(mine + 16 * (0 ^ x)), c1 = *reinterpret_cast<const uint4*>(mine + 16 * (1 ^ x)),
-                        c2 = *reinterpret_cast<const uint4*>(mine + 16 * (2 ^ x)), c3 = *reinterpret_cast<const uint4*>(mine + 16 * (3 ^ x));
-            __syncwarp();
-            const u32 all[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
-#pragma unroll
-            for (int a = 0; a <= RPT; ++a) W[a] = all[a & 15];
+            stage_unit(Ln, W);
             if (u + nw < ue) load_unit(rn, sn, Ln);
         } else {
 #pragma unroll

@@ -51,6 +51,19 @@ __device__ __forceinline__ void fill_table_i8_nt(u32* tab, const u16* pairs) {
     }
 }
 
+// The same fill by nt threads (a multiple of 8) of index i = 0 .. nt - 1 of the block.
+__device__ __forceinline__ void fill_table_i8_span(u32* tab, const u16* pairs, int i, int nt) {
+    uint4* t4 = reinterpret_cast<uint4*>(tab);
+    const int slot = i & 7;
+#pragma unroll 4
+    for (int k = i >> 3; k < 512; k += nt >> 3) {
+        const u32 p = pairs[k];
+        const u32 ep = p & 0xffffu, en = ((0u - p) & 0xffu) | (p & 0xff00u);
+        t4[k * 8 + slot] = make_uint4(ep, ep, ep, ep);
+        t4[(k + 512) * 8 + slot] = make_uint4(en, en, en, en);
+    }
+}
+
 __device__ __forceinline__ void build_table_i8(u32* tab, u16* pairs, const i8* __restrict__ t8) {
     stage_pairs(pairs, t8);
     fill_table_i8(tab, pairs);
