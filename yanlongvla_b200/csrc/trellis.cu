@@ -160,9 +160,10 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
 }
 
 // FX (M <= 4): the layer's pre runs in the kernel: after the dependency wait every CTA rotates and quantizes the M
-// activation rows x (BF16 / F16 / F32) itself (the same row_walsh and quantize_store as k_pre, so the same bits) into
-// shared memory, and the decode loop reads its activations and token scales from there; the separate pre launch and
-// its global round trip disappear.
+// activation rows x (BF16 / F16 / F32) itself (the same transform and quantize_store as the pre kernels, so the same
+// bits) into shared memory, and the decode loop reads its activations and token scales from there; the separate pre
+// launch and its global round trip disappear. With one token and a power-of-two K the transform's threads start at
+// once while the others build the table.
 template <int MT, int LT, bool FX>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tcq(const u16* __restrict__ bits, const i8* __restrict__ t8, const int* __restrict__ q4, const float* __restrict__ s,
