@@ -978,8 +978,16 @@ int dispatch(const int8_t* q, const int8_t* W, void* out, const float* s_tok, co
              cudaStream_t st, const u16* bias = nullptr, const u16* lut = nullptr) {
     const int ct = (N + BM - 1) / BM, half = sms() / 2, KB = (K + BK - 1) / BK;
     auto tiles = [&](int bn) { return ct * ((M + bn - 1) / bn); };
-    // Large products: the two-SM 256 x 256 tile once every SM pair gets a tile.
-    if (M >= 512 && ((N + 255) / 256) * ((M + 255) / 256) >= half) return launch_i8_2sm<MODE>(q, W, out, s_tok, s_ch, M, N, K, st, bias, lut);
+    // Large products: the two-SM 256 x 256 tile once every SM pair gets a tile, unless its last round is so partial
+    // that one-SM 128 x 128 tiles fill the rounds far better (wave efficiency = tiles / (rounds x slots)); the one-SM
+    // tile runs at a lower rate per SM, so smaller differences keep the two-SM tile (measured: 4096 x 4304 -> 1152,
+    // 0.54 against 0.97, 35.0 -> 32.6 us; 1024 x 2048 -> 6144, 0.65 against 0.86, 19.4 -> 22.5 us).
+    auto wave = [](long long t, long long slots) { return (double)t / (double)(((t + slots - 1) / slots) * slots); };
+    const long long t2 = (long long)((N + 255) / 256) * ((M + 255) / 256);
+    if (M >= 512 && t2 >= half) {
+        if (wave(tiles(128), sms()) > wave(t2, half) + 0.3) return launch_i8<128, 6, MODE>(q, W, out, s_tok, s_ch, M, N, K, 1, st, bias, lut);
+        return launch_i8_2sm<MODE>(q, W, out, s_tok, s_ch, M, N, K, st, bias, lut);
+    }
     // Token tiles of 256 on at most half the SMs: tiles of 128 instead while they still fit in one round (twice the
     // SMs at half the work each; measured faster at every such shape of 256-1024 tokens).
     if (M > 128 && tiles(256) >= sms() / 4 && tiles(256) <= half && tiles(128) <= sms())
