@@ -25,7 +25,8 @@ import torch
 from ._lib import DT_BF16, DT_F16, DT_F32, DT_I32, TcqError, check, lib
 
 __all__ = ['quantize', 'pre', 'post', 'post3', 'postg', 'pre2', 'mid2', 'mid1', 'mid2_available', 'decode', 'decode_bf16', 'gemm_w8',
-           'gemm_tcq', 'gemm_tcq_tc', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'int8_gemm_bias', 'device_error', 'gelu_table', 'silu_table', 'act_table',
+           'gemm_tcq', 'gemm_tcq_x', 'gemm_tcq_tc', 'gemmf_tcq', 'gemmf_w8', 'add_norm', 'chain', 'rope', 'workspace',
+           'selftest_wait_expiry', 'pre_h', 'rotate', 'int_mm', 'int8_gemm', 'int8_gemm_bias', 'device_error', 'gelu_table', 'silu_table', 'act_table',
            'TcqError', 'LAUNCHES']
 
 _DT = {torch.bfloat16: DT_BF16, torch.float32: DT_F32, torch.float16: DT_F16, torch.int32: DT_I32}
